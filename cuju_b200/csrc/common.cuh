@@ -14,7 +14,7 @@
 
 #if defined(__CUDACC__)
 #define CB_HD __host__ __device__ __forceinline__
-#define CB_HDNI __host__ __device__ __noinline__
+#define CB_HDNI __host__ __device__ __noinline__ inline
 #define CB_FN __host__ __device__
 #else
 #define CB_HD inline

@@ -1,0 +1,79 @@
+// cuju-b200: the batch kernels. One warp per environment: the lanes run an environment's serial
+// code together and split its data-parallel loops (warp.cuh). The host launches them through the
+// wrappers at the end, on the caller's stream.
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+
+namespace cb {
+
+// A failed environment stops; the first failure code of the batch goes to `anyFail`.
+__device__ __forceinline__ void report(const Batch &b, int e) {
+    if (lane_id() == 0 && b.status[e] != kStatusOk) atomicCAS(b.anyFail, 0, b.status[e]);
+}
+
+__global__ void __launch_bounds__(kThreadsPerBlock) step_kernel(Batch b, const int32_t *__restrict__ actions) {
+    const int e = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (e >= b.count) return;
+    warp_begin();
+    if (b.status[e] != kStatusOk) return;
+    step_environment(b, e, actions);
+    report(b, e);
+}
+
+// Resets every environment whose mask entry is set (all for a null mask).
+__global__ void __launch_bounds__(kThreadsPerBlock) reset_kernel(Batch b, const uint8_t *__restrict__ mask,
+                                                                 const int64_t *__restrict__ seeds,
+                                                                 const int32_t *__restrict__ reverse) {
+    const int e = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (e >= b.count) return;
+    if (mask && !mask[e]) return;
+    warp_begin();
+    if (b.status[e] != kStatusOk) return;
+    reset_and_write(b, e, seeds, reverse);
+    report(b, e);
+}
+
+// Rewrites the outputs of the masked environments from their observations (after a state load).
+__global__ void __launch_bounds__(kThreadsPerBlock) output_kernel(Batch b, const uint8_t *__restrict__ mask) {
+    const int e = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (e >= b.count) return;
+    if (mask && !mask[e]) return;
+    warp_begin();
+    write_env_outputs(b, e, false);
+}
+
+static unsigned grid_for(int count) {
+    const long long threads = (long long)count * 32;
+    return (unsigned)((threads + kThreadsPerBlock - 1) / kThreadsPerBlock);
+}
+
+cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream) {
+    step_kernel<<<grid_for(b.count), kThreadsPerBlock, 0, stream>>>(b, actions);
+    return cudaGetLastError();
+}
+cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse,
+                         cudaStream_t stream) {
+    reset_kernel<<<grid_for(b.count), kThreadsPerBlock, 0, stream>>>(b, mask, seeds, reverse);
+    return cudaGetLastError();
+}
+cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t stream) {
+    output_kernel<<<grid_for(b.count), kThreadsPerBlock, 0, stream>>>(b, mask);
+    return cudaGetLastError();
+}
+cudaError_t kernel_attributes(size_t *localBytes, int *registers) {
+    cudaFuncAttributes a;
+    cudaError_t rc = cudaFuncGetAttributes(&a, step_kernel);
+    if (rc != cudaSuccess) return rc;
+    size_t lb = a.localSizeBytes;
+    int regs = a.numRegs;
+    rc = cudaFuncGetAttributes(&a, reset_kernel);
+    if (rc != cudaSuccess) return rc;
+    if (a.localSizeBytes > lb) lb = a.localSizeBytes;
+    if (a.numRegs > regs) regs = a.numRegs;
+    *localBytes = lb;
+    *registers = regs;
+    return cudaSuccess;
+}
+
+}  // namespace cb

@@ -1,0 +1,21 @@
+// cuju-b200: the launch interface between the host batch (api.cu) and the kernels (kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "env.cuh"
+
+namespace cb {
+
+// Two warps, two environments, per block: small blocks keep the tail of a batch short and let
+// the scheduler fill every SM with the register budget the kernels need.
+constexpr int kThreadsPerBlock = 64;
+
+cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream);
+cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse,
+                         cudaStream_t stream);
+cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t stream);
+// The largest per-thread local memory and register count of the kernels.
+cudaError_t kernel_attributes(size_t *localBytes, int *registers);
+
+}  // namespace cb

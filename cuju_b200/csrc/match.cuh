@@ -303,7 +303,7 @@ CB_HDNI bool match_process(const Sim &s) {
         if (g1 || g2) {
             const int gt = m.lastGoalTeam == 0 ? first : second;
             bool own = true;
-            if (m.lastTouchTeamIDs[kTouchIntentionalKicked] == gt || m.lastTouchTeamIDs[kTouchIntentionalNonKicked] == gt)
+            if (m.lastTouchTeamIDs[kTouchKicked] == gt || m.lastTouchTeamIDs[kTouchNonKicked] == gt)
                 own = false;
             m.lastGoalScorer = team_by_id(w, own ? 1 - gt : gt).lastTouchPlayer;
         }

@@ -5,7 +5,7 @@
 //   camera                              cuju include/cuju/simulation/camera.h:18-167
 #pragma once
 
-#include "humanoid.h"
+#include "humanoid.cuh"
 
 namespace cb {
 

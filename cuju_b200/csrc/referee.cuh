@@ -7,7 +7,6 @@
 
 namespace cb {
 
-enum { kPhasePreMatch, kPhaseFirstHalf, kPhaseSecondHalf };
 
 /// referee.h:26 (BumpActualTime); `t` in milliseconds. Without referee animations the clock skips
 /// the wait of a stoppage at once.

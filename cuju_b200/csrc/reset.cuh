@@ -7,7 +7,6 @@
 
 namespace cb {
 
-constexpr int kFootRight = 1;
 
 /// reset.h:19 (LeftTeamOwnsBall).
 CB_HD bool left_team_owns_ball(const Match &w) {

@@ -1,0 +1,100 @@
+/* cuju-b200: the C-ABI of the B200 batch, a drop-in for the reference CUDA backend
+ * (`libcuju_cuda.so`). Every entry point below has the name, arguments, meaning and error
+ * convention of the reference function cited beside it, so the reference's Python loader binds
+ * this library unchanged (set CUJU_CUDA_LIBRARY to its path).
+ *
+ * Conventions (cuju src/environment_api.h:3-6, 24-31): calls are synchronous unless noted; a
+ * failure returns -1 or null, and `cuju_last_error` gives the message of the last failed call on
+ * the calling thread. A `stream` is a CUDA stream, or null for the default stream. Buffers live in
+ * device memory and never move until `cuju_environment_destroy`.
+ */
+#ifndef CUJU_B200_H
+#define CUJU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cuju src/environment_api.h:47 */
+#define CUJU_CONFIGURATION_VERSION 2
+
+/* cuju src/environment_api.h:49-95 (field order fixed by python/cuju/_batch/library.py:156-187). */
+typedef struct cuju_configuration {
+    int version;
+    const char *const *assets;
+    int asset_count;
+    const int *assignment;
+    const char *animations;
+    int environment_count;
+    unsigned long long seed;
+    int action_set;
+    int observation;
+    int checkpoints;
+    int numpy_legacy;
+    int auto_reset;
+    int threads;
+    int ticks_per_step;
+    int smm_width, smm_height;
+    int stack;
+    const long long *fixed_seeds;
+    const int *agent_counts;
+    int episode_number;
+    unsigned long long first_index;
+    void *(*allocate)(size_t bytes, void *context);
+    void (*release)(void *pointer, void *context);
+    void *allocator_context;
+    int pin_threads;
+    int numa;
+    int page_aligned;
+} cuju_configuration;
+
+/* environment_api.h:41 */ const char *cuju_last_error(void);
+/* environment_api.h:44; returns "cuda" */ const char *cuju_backend(void);
+/* environment_api.h:98 */ void *cuju_environment_create(const cuju_configuration *settings);
+/* environment_api.h:161 */ int cuju_memory_estimate(const cuju_configuration *settings, unsigned long long *bytes);
+/* environment_api.h:172 */ int cuju_local_memory_bytes(unsigned long long *bytes);
+/* environment_api.h:186 */ unsigned long long cuju_environment_memory_bytes(void *environment);
+/* environment_api.h:191 */ void cuju_environment_destroy(void *environment);
+/* environment_api.h:195 */ int cuju_environment_count(void *environment);
+/* environment_api.h:200; 0 on the GPU */ int cuju_environment_threads(void *environment);
+/* environment_api.h:206 */ int cuju_environment_agents(void *environment, int *left, int *right);
+/* environment_api.h:218 */ int cuju_environment_players(void *environment, int *left, int *right);
+/* environment_api.h:229 */ int cuju_environment_set_difficulty(void *environment, const float *difficulty);
+/* environment_api.h:240 */ void cuju_environment_difficulty(void *environment, float *difficulty);
+/* environment_api.h:250 */ int cuju_environment_reset(void *environment, const unsigned int *seeds,
+                                                        const int *reverse, void *stream);
+/* environment_api.h:269 */ int cuju_environment_reset_masked(void *environment, const unsigned char *mask,
+                                                               int mask_on_device, const int64_t *seeds,
+                                                               const int *reverse, void *stream, int synchronize);
+/* environment_api.h:287 */ int cuju_environment_reset_done(void *environment, void *stream);
+/* environment_api.h:302; -2 for a host action outside [-n, n) */
+int cuju_environment_step(void *environment, const int *actions, int on_device, void *stream, int synchronize);
+/* environment_api.h:323 */ int cuju_environment_step_async(void *environment, const int *actions, int on_device,
+                                                             void *stream);
+/* environment_api.h:341 */ int cuju_environment_step_wait(void *environment);
+/* environment_api.h:353 */ int cuju_environment_synchronize(void *environment, void *stream);
+/* environment_api.h:367 */ const char *cuju_environment_get_state(void *environment, int index,
+                                                                    unsigned long long *size, int *episode);
+/* environment_api.h:392 */ int cuju_environment_set_state(void *environment, int index, const char *bytes,
+                                                           unsigned long long size, const int *episode);
+/* environment_api.h:410 */ int cuju_environment_set_stack(void *environment, int index, const char *name,
+                                                           const void *frames, unsigned long long size);
+/* environment_api.h:430; names simple115, final_simple115, reward, done, score_reward */
+void *cuju_environment_buffer(void *environment, const char *name);
+/* environment_api.h:449 */ const char *cuju_environment_raw_field(void *environment, int field, int *type,
+                                                                    int *dimensions, unsigned long long *offset);
+/* environment_api.h:470 */ int cuju_environment_episode(void *environment, int index, long long *values,
+                                                         float *difficulty);
+/* environment_api.h:519 */ const char *cuju_environment_scenario(void *environment, int bundle);
+/* src/state_api.h (state field layout and gather); this backend reports them unavailable */
+int cuju_state_layout(void);
+int cuju_state_gather(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUJU_B200_H */
