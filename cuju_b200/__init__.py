@@ -1,0 +1,9 @@
+"""cuju-b200: Google Research Football's batched environment step on NVIDIA B200 (sm_100a).
+
+A drop-in for the reference's CUDA backend: the C-ABI library `lib/libcuju_b200.so` exports the
+reference's `cuju_*` entry points, and `BatchEnvironment` mirrors the reference Python class.
+"""
+
+from .environment import ActionRangeError, BatchEnvironment, LibraryError, bundled_assets, resolve_asset
+
+__all__ = ['ActionRangeError', 'BatchEnvironment', 'LibraryError', 'bundled_assets', 'resolve_asset']

@@ -362,6 +362,10 @@ CB_HDNI bool reset_from_template(const Sim &s, uint32_t seed) {
     return true;
 }
 
+// A restart waits at most a card's 12 s stoppage plus the set-piece preparation (about 150 steps);
+// a state that waits longer is malformed, and the bound keeps a step finite.
+constexpr int kMaxWaitSteps = 2000;
+
 struct EnvCore {
     int32_t previousScoreDifference;
     int32_t previousGameMode;
@@ -375,7 +379,7 @@ CB_HDNI bool core_after_reset(const Sim &s, EnvCore &core) {
     core.previousGameMode = -1;
     core.previousBallOwnedTeam = -1;
     // A reset reaches play within seconds; the bound only guards a malformed template.
-    for (int guard = 0; guard < 100000; guard++) {
+    for (int guard = 0; guard < kMaxWaitSteps; guard++) {
         environment_get_state(s.w, s.ctx, core.observation);
         if (core.observation.isInPlay) return true;
         if (!environment_step(s)) return false;
@@ -412,7 +416,7 @@ CB_HDNI bool core_step(const Sim &s, EnvCore &core, const int *actions, int &rew
     }
     // Play resumes within seconds of game time; the bound only guards a malformed state.
     for (int guard = 0;; guard++) {
-        if (guard > 100000) return s.fail(kStatusUnsupported);
+        if (guard > kMaxWaitSteps) return s.fail(kStatusUnsupported);
         for (int t = 0; t < s.ctx.ticksPerStep; t++)
             if (!game_tick(s)) return false;
         if (w.m.inPlay) {

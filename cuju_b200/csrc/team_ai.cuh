@@ -353,7 +353,8 @@ CB_HDNI bool team_dynamic_roles(const Sim &s, int teamID) {
             }
         int colOfRow[kTeamPlayers];
         int total = hungarian_solve(cost, n, colOfRow);
-        if (total != -1 && (total < 50000 || cutoff >= nn - 5)) {
+        // The size comparison is unsigned: below five entries `size - 5` wraps and never holds.
+        if (total != -1 && (total < 50000 || (unsigned)cutoff >= (unsigned)nn - 5u)) {
             for (int pi = 0; pi < n; pi++)
                 for (int si = 0; si < n; si++)
                     if (colOfRow[si] == pi) {

@@ -1,0 +1,312 @@
+"""`BatchEnvironment`: the reference's batched GRF environment API on the B200 library.
+
+Names, arguments and results follow the reference class `cuju.BatchEnvironment`
+(python/cuju/_batch/environment.py:270-1560) for the simple115 representations: one reset or step
+of the whole batch per call, outputs as zero-copy views of device buffers, automatic reset with
+`final_observation`, and `get_state` bytes in GRF's format (a pickle of the episode logic, then the
+engine state; python/cuju/_batch/state.py:44-77).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import struct
+from typing import Any
+
+import torch
+
+from . import _native
+
+_REPRESENTATIONS = {'simple115': 1, 'simple115v2': 2}
+_ACTION_SETS = {'default': 0, 'v2': 1, 'full': 2}
+_ACTION_COUNTS = {0: 19, 1: 20, 2: 33}
+
+
+class LibraryError(RuntimeError):
+    """The library refused a call; the message is the library's."""
+
+
+class ActionRangeError(LibraryError, IndexError):
+    """A host action lies outside [-n, n) for n actions."""
+
+
+def bundled_assets() -> list[str]:
+    """The asset bundles staged with the package, such as `5_vs_5_l0_r0`."""
+    directory = os.path.join(_native.DATA_DIRECTORY, 'assets')
+    if not os.path.isdir(directory):
+        return []
+    return sorted(n[: -len('.cjb')] for n in os.listdir(directory) if n.endswith('.cjb'))
+
+
+def _split_name(name):
+    m = re.fullmatch(r'(.+)_l(\d+)_r(\d+)', name)
+    return None if m is None else (m.group(1), int(m.group(2)), int(m.group(3)))
+
+
+def resolve_asset(asset: str) -> tuple[str, tuple[int, int]]:
+    """The bundle path of a path or `<scenario>_l<left>_r<right>` name, and the agents it asks for
+    (-1 keeps the bundle's), as python/cuju/_batch/assets.py:39 resolves them."""
+    if os.path.isfile(asset):
+        return asset, (-1, -1)
+    directory = os.path.join(_native.DATA_DIRECTORY, 'assets')
+    shipped = os.path.join(directory, asset + '.cjb')
+    if os.path.isfile(shipped):
+        return shipped, (-1, -1)
+    split = _split_name(asset)
+    scenarios = {s[0] for s in map(_split_name, bundled_assets()) if s}
+    if split is None and asset in scenarios:
+        split = (asset, 1, 0)
+    if split:
+        scenario, left, right = split
+        bases = [n for n in bundled_assets() if (_split_name(n) or ('',))[0] == scenario]
+        if bases:
+            base = min(bases, key=lambda n: sum(_split_name(n)[1:]))
+            return os.path.join(directory, base + '.cjb'), (left, right)
+    raise FileNotFoundError(f'expected an asset bundle path or `<scenario>_l<left>_r<right>`, found {asset!r}')
+
+
+class _DeviceArray:
+    """A device buffer as `__cuda_array_interface__`, so torch views it without a copy."""
+
+    def __init__(self, pointer: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {
+            'shape': shape, 'typestr': typestr, 'data': (pointer, False), 'version': 3, 'strides': None,
+        }
+
+
+def _pickle_int(v: int) -> bytes:
+    return b'J' + struct.pack('<i', v)
+
+
+def _pickle_str(v: str) -> bytes:
+    d = v.encode()
+    return b'X' + struct.pack('<I', len(d)) + d
+
+
+def pickle_episode(episode: list[int], collected: list[int] | None) -> bytes:
+    """GRF's state pickle of the episode logic (protocol 2, written by opcode)."""
+    logic = b''.join(
+        _pickle_str(k) + _pickle_int(v)
+        for k, v in zip(('previous_score_diff', 'previous_game_mode', 'prev_ball_owned_team'), episode)
+    )
+    data = (b'\x80\x02}(' + _pickle_str('FootballEnvCore') + b'cgfootball.env.football_env_core\nEnvState\n'
+            + b')\x81}(' + logic + b'ub')
+    if collected is not None:
+        data += _pickle_str('CheckpointRewardWrapper') + b'}(' + b''.join(
+            _pickle_int(a) + _pickle_int(c) for a, c in enumerate(collected) if c) + b'u'
+    return data + b'u.'
+
+
+class BatchEnvironment:
+    """A batch of GRF environments stepped on one B200, one warp per environment."""
+
+    def __init__(
+        self,
+        assets: str | list[str],
+        animations: str | None = None,
+        environment_count: int = 1024,
+        representation: str = 'simple115v2',
+        rewards: str = 'scoring',
+        action_set: str = 'default',
+        seed: int = 0,
+        numpy_legacy: bool = True,
+        auto_reset: bool = True,
+        library: str | None = None,
+        assignment: Any = None,
+        difficulty: list[tuple[float | None, float | None]] | None = None,
+        device: str | torch.device = 'cuda',
+        physics_steps_per_frame: int = 10,
+        stacked: bool = False,
+        game_engine_random_seed: Any = None,
+        squeeze: bool = False,
+        agent_counts: list[tuple[int | None, int | None]] | None = None,
+        episode_number: int = 0,
+        first_index: int = 0,
+    ):
+        if representation not in _REPRESENTATIONS:
+            raise ValueError(f'expected one of {sorted(_REPRESENTATIONS)}, found {representation!r}')
+        if action_set not in _ACTION_SETS:
+            raise ValueError(f'expected one of {sorted(_ACTION_SETS)}, found {action_set!r}')
+        reward_names = [r.strip() for r in rewards.split(',') if r.strip()]
+        if not reward_names or reward_names[0] != 'scoring' or not set(reward_names) <= {'scoring', 'checkpoints'}:
+            raise ValueError(f"expected 'scoring' or 'scoring,checkpoints', found {rewards!r}")
+        self._torch_device = torch.device(device)
+        if self._torch_device.type != 'cuda':
+            raise ValueError('the B200 batch runs on a CUDA device only')
+        if self._torch_device.index is None:
+            self._torch_device = torch.device('cuda', torch.cuda.current_device())
+        self._library = _native.load(library)
+        names = [assets] if isinstance(assets, str) else list(assets)
+        resolved = [resolve_asset(a) for a in names]
+        counts = []
+        for (path, (left, right)), pair in zip(resolved, agent_counts or [(None, None)] * len(resolved)):
+            left = left if pair[0] is None else pair[0]
+            right = right if pair[1] is None else pair[1]
+            counts += [left, right]
+        self._paths = [p.encode() for p, _ in resolved]
+        path_array = (ctypes.c_char_p * len(self._paths))(*self._paths)
+        counts_array = (ctypes.c_int * len(counts))(*counts)
+        assignment_array = None
+        if assignment is not None:
+            assignment_array = (ctypes.c_int * environment_count)(*[int(x) for x in assignment])
+        fixed_array = None
+        if game_engine_random_seed is not None:
+            seeds = game_engine_random_seed
+            if isinstance(seeds, int):
+                seeds = [seeds] * environment_count
+            fixed_array = (ctypes.c_longlong * environment_count)(*[int(x) for x in seeds])
+        self._checkpoints = 'checkpoints' in reward_names
+        self.stacked = bool(stacked)
+        self.squeeze = bool(squeeze)
+        animations_path = (animations or os.path.join(_native.DATA_DIRECTORY, 'animations.bin')).encode()
+        config = _native.Configuration(
+            version=_native.CONFIGURATION_VERSION, assets=path_array, asset_count=len(self._paths),
+            assignment=ctypes.cast(assignment_array, ctypes.c_void_p) if assignment_array else None,
+            animations=animations_path, environment_count=environment_count, seed=seed,
+            action_set=_ACTION_SETS[action_set], observation=_REPRESENTATIONS[representation],
+            checkpoints=int(self._checkpoints), numpy_legacy=int(numpy_legacy), auto_reset=int(auto_reset),
+            threads=0, ticks_per_step=physics_steps_per_frame, smm_width=96, smm_height=72,
+            stack=4 if stacked else 1,
+            fixed_seeds=ctypes.cast(fixed_array, ctypes.c_void_p) if fixed_array else None,
+            agent_counts=ctypes.cast(counts_array, ctypes.c_void_p), episode_number=episode_number,
+            first_index=first_index, allocate=None, release=None, allocator_context=None,
+            pin_threads=0, numa=0, page_aligned=0,
+        )
+        with torch.cuda.device(self._torch_device):
+            handle = self._library.cuju_environment_create(ctypes.byref(config))
+        if not handle:
+            raise LibraryError(self._library.cuju_last_error().decode())
+        self._handle = handle
+        self.environment_count = environment_count
+        left = (ctypes.c_int * environment_count)()
+        right = (ctypes.c_int * environment_count)()
+        self.agents = self._library.cuju_environment_agents(handle, left, right)
+        self.left_agents = torch.tensor(list(left), dtype=torch.int32)
+        self.right_agents = torch.tensor(list(right), dtype=torch.int32)
+        self.action_count = _ACTION_COUNTS[_ACTION_SETS[action_set]]
+        self.torch_device = self._torch_device
+        if difficulty is not None:
+            per_bundle = [(-1.0 if l is None else float(l), -1.0 if r is None else float(r)) for l, r in difficulty]
+            bundle_of = [0] * environment_count if assignment is None else [int(x) for x in assignment]
+            values = (ctypes.c_float * (2 * environment_count))(*[v for b in bundle_of for v in per_bundle[b]])
+            self._check(self._library.cuju_environment_set_difficulty(handle, values))
+        width = 115 * (4 if stacked else 1)
+        self._observation_shape = (environment_count, self.agents, width)
+        self._views = {}
+
+    # -- plumbing ------------------------------------------------------------------------------
+    def _check(self, status: int) -> None:
+        if status == -2:
+            raise ActionRangeError(self._library.cuju_last_error().decode())
+        if status != 0:
+            raise LibraryError(self._library.cuju_last_error().decode())
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self._torch_device).cuda_stream
+
+    def _view(self, name: str, shape: tuple[int, ...], typestr: str, dtype: torch.dtype) -> torch.Tensor:
+        if name not in self._views:
+            pointer = self._library.cuju_environment_buffer(self._handle, name.encode())
+            if not pointer:
+                raise LibraryError(f'the batch has no buffer {name}')
+            self._views[name] = torch.as_tensor(_DeviceArray(pointer, shape, typestr), device=self._torch_device)
+        return self._views[name]
+
+    def _outputs(self):
+        e, a = self.environment_count, self.agents
+        obs = self._view('simple115', self._observation_shape, '<f4', torch.float32)
+        final = self._view('final_simple115', self._observation_shape, '<f4', torch.float32)
+        reward = self._view('reward', (e, a), '<f4', torch.float32)
+        done = self._view('done', (e,), '|b1', torch.bool)
+        score = self._view('score_reward', (e,), '<i4', torch.int32)
+        if self.squeeze and a == 1:
+            obs, final, reward = obs.squeeze(1), final.squeeze(1), reward.squeeze(1)
+        return obs, reward, done, final, score
+
+    # -- the environment API -------------------------------------------------------------------
+    def reset(self, seeds: Any = None, reverse: Any = None, mask: Any = None) -> torch.Tensor:
+        """Starts the next episode of every environment (or of those `mask` selects)."""
+        e = self.environment_count
+        seed_t = None if seeds is None else torch.as_tensor(seeds, dtype=torch.int64).reshape(-1).expand(e).contiguous()
+        rev_t = None if reverse is None else torch.as_tensor(reverse, dtype=torch.int32).reshape(-1).expand(e).contiguous()
+        if seed_t is not None and bool(((seed_t < -1) | (seed_t > 4294967295)).any()):
+            raise ValueError(f'expected seeds from 0 to 4294967295, or -1 to draw, found {seed_t.tolist()}')
+        with torch.cuda.device(self._torch_device):
+            if mask is not None or (seed_t is not None and bool((seed_t == -1).any())):
+                mask_t, on_device = None, 0
+                if mask is not None:
+                    mask_t = torch.as_tensor(mask).to(torch.uint8)
+                    on_device = int(mask_t.is_cuda)
+                    mask_t = mask_t.contiguous()
+                self._check(self._library.cuju_environment_reset_masked(
+                    self._handle, None if mask_t is None else mask_t.data_ptr(), on_device,
+                    None if seed_t is None else seed_t.data_ptr(),
+                    None if rev_t is None else rev_t.data_ptr(), self._stream(), int(mask is None)))
+            else:
+                seeds32 = None if seed_t is None else (ctypes.c_uint * e)(*[int(x) for x in seed_t.tolist()])
+                self._check(self._library.cuju_environment_reset(
+                    self._handle, seeds32, None if rev_t is None else rev_t.data_ptr(), self._stream()))
+        return self._outputs()[0]
+
+    def reset_done(self) -> None:
+        """Starts the next episode of every environment whose episode ended (auto_reset off)."""
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_reset_done(self._handle, self._stream()))
+
+    def step(self, actions: Any, synchronize: bool = True):
+        """One step of every environment: returns observation, reward, done and an info dict
+        with `final_observation` and `score_reward`."""
+        a = torch.as_tensor(actions)
+        if a.dim() == 1:
+            a = a.reshape(self.environment_count, -1)
+        a = a.to(torch.int32).contiguous()
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_step(
+                self._handle, a.data_ptr(), int(a.is_cuda), self._stream(), int(synchronize)))
+        obs, reward, done, final, score = self._outputs()
+        return obs, reward, done, {'final_observation': final, 'score_reward': score}
+
+    def synchronize(self) -> None:
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_synchronize(self._handle, self._stream()))
+
+    def engine_state(self, index: int) -> tuple[bytes, list[int]]:
+        """The engine bytes of environment `index` and its episode values (3 + agents)."""
+        episode = (ctypes.c_int * (3 + _native.MAXIMUM_AGENTS))()
+        size = ctypes.c_ulonglong()
+        torch.cuda.synchronize(self._torch_device)
+        with torch.cuda.device(self._torch_device):
+            pointer = self._library.cuju_environment_get_state(self._handle, index, ctypes.byref(size), episode)
+        if not pointer:
+            raise LibraryError(self._library.cuju_last_error().decode())
+        return ctypes.string_at(pointer, size.value), list(episode)
+
+    def get_state(self, index: int) -> bytes:
+        """The state of environment `index` in GRF's byte format (episode pickle, then engine)."""
+        match, episode = self.engine_state(index)
+        collected = episode[3: 3 + self.agents] if self._checkpoints else None
+        data = pickle_episode(episode[:3], collected)
+        return struct.pack('<i', len(data)) + data + match
+
+    def episode(self, index: int) -> list[int]:
+        values = (ctypes.c_longlong * 17)()
+        self._check(self._library.cuju_environment_episode(self._handle, index, values, None))
+        return list(values)
+
+    def memory_bytes(self) -> int:
+        return int(self._library.cuju_environment_memory_bytes(self._handle))
+
+    def close(self) -> None:
+        if getattr(self, '_handle', None):
+            torch.cuda.synchronize(self._torch_device)
+            self._views.clear()
+            self._library.cuju_environment_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

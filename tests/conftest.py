@@ -1,0 +1,109 @@
+"""Shared helpers of the parity tests.
+
+The parity bar is bit-exactness: every observation, reward and done flag of every step, and every
+environment's GRF state bytes, equal the reference's (its published digests in
+tests/golden/digests.json, and its CPU backend built from source into oracle/_ref, run live).
+"""
+
+import hashlib
+import json
+import os
+import sys
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, 'tests', 'golden', 'digests.json')
+DATA = os.path.join(ROOT, 'cuju_b200', 'data')
+ANIMATIONS = os.path.join(DATA, 'animations.bin')
+
+
+def pytest_configure(config):
+    config.addinivalue_line('markers', 'gpu: needs a CUDA device (a B200) and the built library')
+
+
+def golden():
+    with open(GOLDEN, encoding='utf-8') as handle:
+        return json.load(handle)
+
+
+def actions_at(step, environments, agents, action_count):
+    """The actions of a step from integer arithmetic alone (cuju tests/conftest.py:60-66)."""
+    return [[(step * 7 + e * 3 + a * 5) % action_count for a in range(agents)] for e in range(environments)]
+
+
+def resolve(assets):
+    """Bundle paths and per-bundle agent counts of an asset name or list of names."""
+    from cuju_b200.environment import resolve_asset
+
+    names = [assets] if isinstance(assets, str) else list(assets)
+    resolved = [resolve_asset(n) for n in names]
+    return [p for p, _ in resolved], [c for _, c in resolved]
+
+
+def tensor_bytes(tensor):
+    tensor = tensor.detach().to('cpu').contiguous()
+    return tensor.numpy().tobytes()
+
+
+def device_digest(assets, steps, seed=7, environments=4, **options):
+    """The golden digest of a run of the B200 batch (cuju tests/conftest.py:69-99)."""
+    from cuju_b200 import BatchEnvironment
+
+    batch = BatchEnvironment(assets, environment_count=environments, seed=seed, **options)
+    digest = hashlib.sha256()
+    digest.update(tensor_bytes(batch.reset()))
+    for step in range(steps):
+        actions = torch.tensor(actions_at(step, environments, batch.agents, batch.action_count), dtype=torch.int32)
+        observation, reward, done, _ = batch.step(actions.cuda())
+        digest.update(tensor_bytes(observation))
+        digest.update(tensor_bytes(reward))
+        digest.update(tensor_bytes(done))
+    if not batch.stacked:
+        for index in range(environments):
+            digest.update(batch.get_state(index))
+    batch.close()
+    return digest.hexdigest()
+
+
+def oracle_digest(assets, steps, seed=7, environments=4, **options):
+    """The same digest from the reference CPU backend (oracle/_ref/libcuju_cpu.so)."""
+    import struct
+
+    from cuju_b200.environment import pickle_episode
+    from oracle.driver import OracleBatch
+
+    paths, counts = resolve(assets)
+    checkpoints = 'checkpoints' in options.get('rewards', '')
+    stack = 4 if options.get('stacked') else 1
+    batch = OracleBatch(paths, counts, environments, seed, ANIMATIONS, checkpoints=checkpoints, stack=stack,
+                        assignment=options.get('assignment'))
+    digest = hashlib.sha256()
+    digest.update(batch.reset()[0])
+    for step in range(steps):
+        flat = [x for row in actions_at(step, environments, batch.agents, 19) for x in row]
+        obs, reward, done, _ = batch.step(flat)
+        digest.update(obs)
+        digest.update(reward)
+        digest.update(done)
+    if stack == 1:
+        for index in range(environments):
+            match, episode = batch.engine_state(index)
+            collected = episode[3:3 + batch.agents] if checkpoints else None
+            data = pickle_episode(episode[:3], collected)
+            digest.update(struct.pack('<i', len(data)) + data + match)
+    batch.close()
+    return digest.hexdigest()
+
+
+def simple115_cases():
+    """The golden cases of the representations this backend writes."""
+    cases = golden()['cases']
+    return sorted(name for name, case in cases.items() if case['options'].get('representation') in (None, 'simple115v2', 'simple115'))
+
+
+needs_data = pytest.mark.skipif(not os.path.isfile(ANIMATIONS), reason='run __graft_entry__.build() to stage the data')

@@ -1,0 +1,105 @@
+"""CPU checks: the oracle against the reference's golden digests, the C-ABI library's exports, and
+the host-side logic of the Python mirror. No GPU is needed."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT, golden, needs_data, oracle_digest
+
+HEADER = os.path.join(ROOT, 'include', 'cuju_b200.h')
+LIBRARY = os.path.join(ROOT, 'cuju_b200', 'lib', 'libcuju_b200.so')
+ORACLE = os.path.join(ROOT, 'oracle', '_ref', 'libcuju_cpu.so')
+
+
+def declared_symbols():
+    with open(HEADER, encoding='utf-8') as handle:
+        text = handle.read()
+    return sorted(set(re.findall(r'\b(cuju_[a-z_]+)\s*\(', text)))
+
+
+def test_header_declares_the_reference_entry_points():
+    names = declared_symbols()
+    for required in ('cuju_environment_create', 'cuju_environment_step', 'cuju_environment_reset',
+                     'cuju_environment_reset_masked', 'cuju_environment_get_state', 'cuju_environment_buffer',
+                     'cuju_last_error', 'cuju_backend'):
+        assert required in names
+
+
+@pytest.mark.skipif(not os.path.isfile(LIBRARY), reason='library not built')
+def test_library_loads_and_exports_every_declared_symbol():
+    library = ctypes.CDLL(LIBRARY)
+    missing = [name for name in declared_symbols() if not hasattr(library, name)]
+    assert missing == []
+    library.cuju_backend.restype = ctypes.c_char_p
+    assert library.cuju_backend() == b'cuda'
+
+
+@pytest.mark.skipif(not os.path.isfile(LIBRARY), reason='library not built')
+def test_library_rejects_a_wrong_configuration_version_without_a_device():
+    from cuju_b200 import _native
+
+    library = _native.declare(ctypes.CDLL(LIBRARY))
+    config = _native.Configuration(version=1)
+    assert not library.cuju_environment_create(ctypes.byref(config))
+    assert b'configuration version 2' in library.cuju_last_error()
+
+
+def test_pickle_of_the_episode_logic_is_grf_protocol_2():
+    import pickle
+
+    from cuju_b200.environment import pickle_episode
+
+    class EnvState:
+        pass
+
+    class Unpickler(pickle.Unpickler):
+        def find_class(self, module, name):
+            assert (module, name) == ('gfootball.env.football_env_core', 'EnvState')
+            return EnvState
+
+    import io
+
+    data = Unpickler(io.BytesIO(pickle_episode([1, 0, -1], [0, 3]))).load()
+    assert data['FootballEnvCore'].__dict__ == {'previous_score_diff': 1, 'previous_game_mode': 0,
+                                                'prev_ball_owned_team': -1}
+    assert data['CheckpointRewardWrapper'] == {1: 3}
+
+
+@needs_data
+def test_asset_names_resolve_to_bundles_and_agent_counts():
+    from cuju_b200.environment import resolve_asset
+
+    path, counts = resolve_asset('5_vs_5_l4_r0')
+    assert path.endswith('5_vs_5_l0_r0.cjb') and counts == (4, 0)
+    path, counts = resolve_asset('academy_corner')
+    assert path.endswith('academy_corner_l0_r0.cjb') and counts == (1, 0)
+    with pytest.raises(FileNotFoundError):
+        resolve_asset('no_such_scenario_l1_r0')
+
+
+# The oracle (the reference CPU backend built from source) reproduces the reference's published
+# digests: the pin of every parity test. A sample that runs in seconds; the rest run on the GPU box.
+ORACLE_CASES = ['5_vs_5/simple115v2', 'academy_empty_goal_close/simple115v2', '1_vs_1_easy/simple115v2',
+                'mixed', '11_vs_11_stochastic/checkpoints', '5_vs_5/stacked']
+
+
+@needs_data
+@pytest.mark.skipif(not os.path.isfile(ORACLE), reason='oracle not built')
+@pytest.mark.parametrize('case', ORACLE_CASES)
+def test_oracle_matches_the_golden_digest(case):
+    g = golden()
+    entry = g['cases'][case]
+    assert oracle_digest(entry['assets'], g['steps'], seed=g['seed'], environments=g['environments'],
+                         **entry['options']) == entry['digest']
+
+
+@needs_data
+@pytest.mark.skipif(not os.path.isfile(ORACLE), reason='oracle not built')
+def test_a_planted_difference_changes_the_oracle_digest():
+    # The digest is sensitive: one more step, or another seed, gives another digest.
+    g = golden()
+    entry = g['cases']['1_vs_1_easy/simple115v2']
+    assert oracle_digest(entry['assets'], g['steps'], seed=g['seed'] + 1, environments=g['environments']) != entry['digest']
