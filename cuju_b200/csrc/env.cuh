@@ -610,7 +610,7 @@ CB_HDNI bool reset_environment(const Batch &b, int e, const int64_t *seeds, cons
     EnvSlot &slot = b.slots[e];
     // Lane 0 keeps the books; the other lanes read them after the barrier.
     wsync();
-    if (lane_id() == 0) {
+    if (leader()) {
         const bool given = seeds && seeds[e] >= 0;
         const bool fixed = slot.fixedSeed >= 0;
         const bool deterministic = b.variants[slot.bundle * 4].tmpl->scenario.deterministic;
@@ -688,7 +688,7 @@ CB_HDNI void write_env_outputs(const Batch &b, int e, bool afterStep) {
 
 CB_HDNI bool reset_and_write(const Batch &b, int e, const int64_t *seeds, const int32_t *reverse) {
     if (!reset_environment(b, e, seeds, reverse)) return false;
-    if (lane_id() == 0) b.done[e] = 0;
+    if (leader()) b.done[e] = 0;
     write_env_outputs(b, e, false);
     return true;
 }
@@ -701,7 +701,7 @@ CB_HDNI bool step_environment(const Batch &b, int e, const int32_t *actions) {
     const int agents = slot.leftAgents + slot.rightAgents;
     if (!b.autoReset && b.done[e]) {
         wsync();
-        if (lane_id() == 0) {
+        if (leader()) {
             for (int a = 0; a < b.agents; a++) b.reward[(size_t)e * b.agents + a] = 0.0f;
             b.scoreReward[e] = 0;
         }
@@ -725,14 +725,14 @@ CB_HDNI bool step_environment(const Batch &b, int e, const int32_t *actions) {
     wsync();
     update_sticky(b, w, slot);
     wsync();
-    if (lane_id() == 0) {
+    if (leader()) {
         for (int a = 0; a < b.agents; a++)
             b.reward[(size_t)e * b.agents + a] = a < agents ? (float)(a < slot.leftAgents ? reward : -reward) : 0.0f;
         b.done[e] = done;
         b.scoreReward[e] = reward;
     }
     write_env_outputs(b, e, true);
-    if (done && lane_id() == 0)
+    if (done && leader())
         for (int t = 0; t < 2; t++) slot.finalDesignated[t] = b.cores[e].observation.team[t].designatedPlayer;
     wsync();
     if (!b.autoReset || !done) return true;

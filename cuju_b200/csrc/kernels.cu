@@ -1,6 +1,7 @@
-// cuju-b200: the batch kernels. One warp per environment: the lanes run an environment's serial
-// code together and split its data-parallel loops (warp.cuh). The host launches them through the
-// wrappers at the end, on the caller's stream.
+// cuju-b200: the batch kernels. One lane per environment: each thread runs its environment's
+// whole step (every warp-cooperative construct of warp.cuh runs serially on the lane), so a warp
+// advances 32 environments at once and a batch of 16,384 is resident in one wave. The host
+// launches them through the wrappers at the end, on the caller's stream.
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -9,14 +10,14 @@ namespace cb {
 
 // A failed environment stops; the first failure code of the batch goes to `anyFail`.
 __device__ __forceinline__ void report(const Batch &b, int e) {
-    if (lane_id() == 0 && b.status[e] != kStatusOk) atomicCAS(b.anyFail, 0, b.status[e]);
+    if (b.status[e] != kStatusOk) atomicCAS(b.anyFail, 0, b.status[e]);
 }
+__device__ __forceinline__ int env_index() { return (int)(blockIdx.x * blockDim.x + threadIdx.x); }
 
 __global__ void __launch_bounds__(kThreadsPerBlock) step_kernel(Batch b, const int32_t *__restrict__ actions) {
-    const int e = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (e >= b.count) return;
-    warp_begin();
-    if (b.status[e] != kStatusOk) return;
+    lane_mode_begin();
+    const int e = env_index();
+    if (e >= b.count || b.status[e] != kStatusOk) return;
     step_environment(b, e, actions);
     report(b, e);
 }
@@ -25,27 +26,23 @@ __global__ void __launch_bounds__(kThreadsPerBlock) step_kernel(Batch b, const i
 __global__ void __launch_bounds__(kThreadsPerBlock) reset_kernel(Batch b, const uint8_t *__restrict__ mask,
                                                                  const int64_t *__restrict__ seeds,
                                                                  const int32_t *__restrict__ reverse) {
-    const int e = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (e >= b.count) return;
-    if (mask && !mask[e]) return;
-    warp_begin();
-    if (b.status[e] != kStatusOk) return;
+    lane_mode_begin();
+    const int e = env_index();
+    if (e >= b.count || (mask && !mask[e]) || b.status[e] != kStatusOk) return;
     reset_and_write(b, e, seeds, reverse);
     report(b, e);
 }
 
 // Rewrites the outputs of the masked environments from their observations (after a state load).
 __global__ void __launch_bounds__(kThreadsPerBlock) output_kernel(Batch b, const uint8_t *__restrict__ mask) {
-    const int e = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (e >= b.count) return;
-    if (mask && !mask[e]) return;
-    warp_begin();
+    lane_mode_begin();
+    const int e = env_index();
+    if (e >= b.count || (mask && !mask[e])) return;
     write_env_outputs(b, e, false);
 }
 
 static unsigned grid_for(int count) {
-    const long long threads = (long long)count * 32;
-    return (unsigned)((threads + kThreadsPerBlock - 1) / kThreadsPerBlock);
+    return (unsigned)((count + kThreadsPerBlock - 1) / kThreadsPerBlock);
 }
 
 cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream) {

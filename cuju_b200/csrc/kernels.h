@@ -7,8 +7,8 @@
 
 namespace cb {
 
-// Two warps, two environments, per block: small blocks keep the tail of a batch short and let
-// the scheduler fill every SM with the register budget the kernels need.
+// Two warps (64 environments) per block: small blocks keep the tail of a batch short and let the
+// scheduler fill every SM with the register budget the kernels need.
 constexpr int kThreadsPerBlock = 64;
 
 cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream);

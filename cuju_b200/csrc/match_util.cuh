@@ -62,13 +62,14 @@ enum StepStatus : int32_t {
     kStatusOverflow = 2,      // a fixed-capacity list would overflow
 };
 
-// The per-step scratch of one warp (global memory, one per environment).
+// The sort scratch of one environment (global memory): bitonic pairs for a warp-wide sort, or
+// the two key/position buffers of a merge sort when one lane owns the environment.
 struct alignas(16) WarpScratch {
     double keys[2048];
     int16_t idx[2048];
     int16_t list[1536];
-    Vec3 positions[kAnimPositions];  // candidate physics positions
-    Vec3 positions2[kAnimPositions];
+    double keys2[1536];
+    int16_t idx2[1536];
 };
 
 // Everything a simulation function needs: the match, its context and the warp's scratch.

@@ -187,8 +187,50 @@ CB_HDNI void stable_sort(const Sim &s, AnimList &list, KeyFn key) {
         return;
     }
 #endif
-    (void)s;
-    // Serial stable insertion sort (nested or host use).
+    if (lane_env() && s.scratch) {
+        // The lane owns the environment's scratch: each key once, then a bottom-up stable merge
+        // sort of (key, position) runs, the left run winning ties.
+        WarpScratch &sc = *s.scratch;
+        double *ka = sc.keys, *kb = sc.keys2;
+        int16_t *ia = sc.idx, *ib = sc.idx2;
+        for (int i = 0; i < n; i++) {
+            ka[i] = (double)key((int)list[i]);
+            ia[i] = list[i];
+        }
+        for (int width = 1; width < n; width *= 2) {
+            for (int lo = 0; lo < n; lo += 2 * width) {
+                const int mid = lo + width < n ? lo + width : n;
+                const int hi = lo + 2 * width < n ? lo + 2 * width : n;
+                int l = lo, r = mid, o = lo;
+                while (l < mid && r < hi) {
+                    if (ka[r] < ka[l]) {
+                        kb[o] = ka[r];
+                        ib[o++] = ia[r++];
+                    } else {
+                        kb[o] = ka[l];
+                        ib[o++] = ia[l++];
+                    }
+                }
+                while (l < mid) {
+                    kb[o] = ka[l];
+                    ib[o++] = ia[l++];
+                }
+                while (r < hi) {
+                    kb[o] = ka[r];
+                    ib[o++] = ia[r++];
+                }
+            }
+            double *kt = ka;
+            ka = kb;
+            kb = kt;
+            int16_t *it = ia;
+            ia = ib;
+            ib = it;
+        }
+        for (int i = 0; i < n; i++) list[i] = ia[i];
+        return;
+    }
+    // Serial stable insertion sort (nested inside a warp-shared environment).
     for (int i = 1; i < n; i++) {
         int16_t v = list[i];
         double kv = (double)key((int)v);

@@ -24,6 +24,13 @@ CB_HD void warp_begin() {
     __syncwarp();
 }
 CB_HD bool in_region() { return region_flag() != 0; }
+// Set when each lane owns an environment of its own: every construct then runs serially on its
+// lane, and per-environment scratch belongs to the lane.
+CB_HD void lane_mode_begin() { region_flag() = 2; }
+CB_HD bool lane_env() { return region_flag() == 2; }
+// The lane that stores an environment's books: lane 0 of a warp that shares one environment, or
+// every lane when each owns its own.
+CB_HD bool leader() { return lane_env() || lane_id() == 0; }
 CB_HD void region_enter() {
     __syncwarp();
     if (lane_id() == 0) region_flag() = 1;
@@ -48,6 +55,9 @@ CB_HD void wsync() {
 CB_HD int lane_id() { return 0; }
 CB_HD void warp_begin() {}
 CB_HD bool in_region() { return true; }
+CB_HD void lane_mode_begin() {}
+CB_HD bool lane_env() { return true; }
+CB_HD bool leader() { return true; }
 CB_HD void split(bool &nested, int &lane, int &stride) { nested = true; lane = 0; stride = 1; }
 CB_HD void wsync() {}
 #endif
