@@ -113,7 +113,8 @@ struct AIController {
         if (m.ballRetainer >= 0) return;
         if (fabsf(ball(160).c[1]) > 20.05f) return;
         if ((double)(ball(160).c[0] * -side) > -(double)kPitchHalfL + 16.4) return;
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.desiredFunctionType = kFtDeflect;
         c.useDesiredMovement = false;
         c.useDesiredLookAt = false;
@@ -121,7 +122,8 @@ struct AIController {
         push(c);
     }
     CB_HDNI void set_piece_command() {
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.desiredFunctionType = kFtMovement;
         c.useDesiredMovement = true;
         c.useDesiredLookAt = true;
@@ -142,7 +144,8 @@ struct AIController {
         }
         if (m.designatedPossessionPlayer == player ||
             (team().designatedTeamPossessionPlayer == player && duel_likeliness() >= 0.25f)) {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtBallControl;
             c.useDesiredMovement = true;
             c.desiredDirection = ctl.inputDirection;
@@ -177,7 +180,8 @@ struct AIController {
             (m.designatedPossessionPlayer == player ||
              (team().designatedTeamPossessionPlayer == player && pl.timeNeededToGetToBallOptimistic_ms < 1000 &&
               ctl.oppTimeNeededToGetToBall > 400 && !ctl.oppTeamHasPossession && duel_likeliness() >= 0.5f))) {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtTrap;
             c.useDesiredMovement = true;
             c.desiredDirection = ctl.inputDirection;
@@ -199,7 +203,8 @@ struct AIController {
         if (m.ballRetainer >= 0) return;
         if (ctl.teamHasBestPossession) return;
         if (!byAnyMeans && duel_likeliness() < 0.2f) return;
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.desiredFunctionType = kFtInterfere;
         c.useDesiredMovement = true;
         c.strictMovement = byAnyMeans ? kStrictFalse : kStrictTrue;
@@ -221,7 +226,8 @@ struct AIController {
         const AnimationState &oa = hum(w, o).anim;
         if ((bd > 0.7f && bd < 1.6f && ctl.oppTimeNeededToGetToBall > 260) ||
             (bd > 0.6f && bd < 1.8f && oa.functionType == kFtShot && oa.frameNumber < oa.touchFrame)) {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtSliding;
             c.useDesiredMovement = true;
             c.desiredDirection = ((bp.flat() + mov(o) * 0.2f) - pp).normalized(Vec3(-side, 0, 0));
@@ -392,7 +398,8 @@ struct AIController {
         const int lookT = 40;
         Vec3 qid = ctl.inputDirection;
         quantize_direction(qid, kQuantizedDirBias);
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.desiredFunctionType = kFtMovement;
         c.useDesiredMovement = true;
         c.useDesiredLookAt = true;
@@ -577,7 +584,8 @@ struct AIController {
             sp.power = 2.0f * runW;
             field_push(s, ff, sp);
         }
-        PlayerList opps = closest_players(s, oppID, mainMan * 0.3f + cur + 0.7f, false, 3);
+        PlayerList opps;
+        closest_players(opps, s, oppID, mainMan * 0.3f + cur + 0.7f, false, 3);
         for (int i = 0; i < opps.count; i++) {
             PlayerImage oi = mental_player_image(w, mi, opps[i]);
             ForceSpot sp;
@@ -595,7 +603,8 @@ struct AIController {
             field_push(s, ff, sp);
         }
         if (team().fadingTeamPossessionAmount >= 1.02f) {
-            PlayerList mates = closest_players(s, teamID, cur, false, 6);
+            PlayerList mates;
+            closest_players(mates, s, teamID, cur, false, 6);
             for (int i = 0; i < mates.count; i++) {
                 if (mates[i] == player) continue;
                 PlayerImage mimg = mental_player_image(w, mi, mates[i]);
@@ -829,7 +838,8 @@ struct AIController {
         return passing_odds(tp, passType, opps);
     }
     CB_HDNI void add_pass(int target, int passType) {
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.desiredFunctionType = passType;
         c.useDesiredMovement = false;
         c.useDesiredLookAt = false;
@@ -850,7 +860,8 @@ struct AIController {
                         .normalized(Vec3(0)) +
                     Vec3(0, 0, 0.3f);
         away.normalize(dir());
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.useDesiredMovement = false;
         c.useDesiredLookAt = false;
         c.touchInfo.inputDirection = away;
@@ -875,7 +886,8 @@ struct AIController {
         float offF = 0.7f + kDribbleOffensiveness * 0.05f + mind_set(dynamic_role()) * 0.05f;
         float pm = 1.0f;
         float fut = 0.25f;
-        PlayerList opps = closest_players(s, oppID, mp, false, 5);
+        PlayerList opps;
+        closest_players(opps, s, oppID, mp, false, 5);
         List<PlayerImage, kPlayers> imgs;
         for (int i = 0; i < opps.count; i++) imgs.push(mental_player_image(w, mi, opps[i]));
         float nb = nclamp(fabsf(mp.c[0]) / kPitchHalfL, 0.0f, 1.0f);
@@ -939,7 +951,8 @@ struct AIController {
         const TacticalSituation &sit = pl.tactical;
         float tr = sit.forwardSpaceRating * fsW + sit.spaceRating * sW + sit.forwardRating * fW;
         tr /= totalTW;
-        PlayerList mates = active_players(w, teamID);
+        PlayerList mates;
+        active_players(mates, w, teamID);
         float bestTotal = 0.0f;
         int bestP = -1;
         float bestPassR = 0.0f;
@@ -1007,7 +1020,8 @@ struct AIController {
             }
             odds = lm::lm_powf(odds, 0.5f);
             if (odds + rnd(0.0f, 0.5f) > 0.5f) {
-                PlayerCommand c = default_command();
+                PlayerCommand c;
+                default_command(c);
                 c.desiredFunctionType = kFtShot;
                 c.useDesiredMovement = false;
                 c.useDesiredLookAt = false;
@@ -1058,7 +1072,8 @@ struct AIController {
         }
         const uint64_t stop = m.referee.buffer.stopTime;
         if (m.actualTime_ms - stop > 2000 && m.actualTime_ms - stop < 4000) {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtSpecial;
             c.useSpecialVar1 = true;
             c.specialVar1 = ct;
@@ -1068,7 +1083,8 @@ struct AIController {
             c.useDesiredLookAt = false;
             push(c);
         }
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.desiredFunctionType = kFtMovement;
         c.useDesiredMovement = true;
         c.desiredDirection = dd;
@@ -1080,7 +1096,8 @@ struct AIController {
 
     CB_HDNI void set_piece_commands() {
         const int spt = team_ai().setPieceType;
-        PlayerCommand ac = default_command();
+        PlayerCommand ac;
+        default_command(ac);
         if (spt == kGmPenalty) {
             ac.desiredFunctionType = kFtShot;
             ac.useDesiredMovement = false;
@@ -1161,14 +1178,16 @@ struct AIController {
             }
         }
         if (m.ballRetainer != player) {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtMovement;
             c.useDesiredMovement = true;
             c.useDesiredLookAt = true;
             ball_control_movement(kWalkVel, c.desiredDirection, c.desiredVelocityFloat, c.desiredLookAt);
             push(c);
         } else {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtMovement;
             c.useDesiredMovement = true;
             c.desiredDirection = (ac.touchInfo.desiredDirection.length() > 0.0f)
@@ -1206,7 +1225,8 @@ struct AIController {
             return true;
         } else if (!m.inPlay && rb.active && (m.referee.foul.foulType == 2 || m.referee.foul.foulType == 3) &&
                    rb.stopTime < m.actualTime_ms - 1000 && rb.prepareTime > m.actualTime_ms) {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtMovement;
             c.useDesiredMovement = true;
             c.useDesiredLookAt = true;
@@ -1216,7 +1236,8 @@ struct AIController {
             push(c);
             return true;
         } else if (!m.inPlay || lazy) {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtMovement;
             c.useDesiredMovement = true;
             c.desiredDirection = (dir() * 0.6f + (Vec3(0) - pos()).normalized(dir()) * 0.4f).normalized(dir());
@@ -1289,7 +1310,8 @@ struct AIController {
                         extraHaste = true;
                     }
                     int huntCount = 2;
-                    PlayerList cp = closest_players(s, teamID, pos(o) + mov(o) * 0.1f, false, huntCount);
+                    PlayerList cp;
+                    closest_players(cp, s, teamID, pos(o) + mov(o) * 0.1f, false, huntCount);
                     bool close = false;
                     for (int i = 0; i < cp.count; i++)
                         if (cp[i] == player) {
@@ -1309,7 +1331,8 @@ struct AIController {
             ctl.inputVelocityFloat = range_velocity(ctl.inputVelocityFloat);
             movement_command(forceMagnet, extraHaste);
         } else {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtMovement;
             c.useDesiredMovement = true;
             c.desiredDirection = manDir;
@@ -1384,7 +1407,8 @@ CB_HDNI bool human_request_command(const Sim &s, int player, CommandQueue &q) {
             float gauge = (float)(hc.gauge_ms - baseTime) * (1.0f / float(1000 - baseTime));
             gauge = clampf_(gauge, 0.0f, 1.0f);
             auto pass = [&](int passType, float exponent, float autoDir, float autoPow) {
-                PlayerCommand c = default_command();
+                PlayerCommand c;
+                default_command(c);
                 c.desiredFunctionType = passType;
                 c.useDesiredMovement = false;
                 c.useDesiredLookAt = false;
@@ -1399,7 +1423,8 @@ CB_HDNI bool human_request_command(const Sim &s, int player, CommandQueue &q) {
                 queue_push(s, q, c);
             };
             if (m.inSetPiece && tai.taker == player && tai.setPieceType == kGmKickOff) {
-                PlayerCommand c = default_command();
+                PlayerCommand c;
+                default_command(c);
                 c.desiredFunctionType = kFtShortPass;
                 TouchInfo &t = c.touchInfo;
                 t.autoDirectionBias = 1.0f;
@@ -1418,7 +1443,8 @@ CB_HDNI bool human_request_command(const Sim &s, int player, CommandQueue &q) {
             } else if (hc.actionButton == kBtnHighPass) {
                 pass(kFtHighPass, 0.55f, 0.2f, 0.5f);
             } else if (hc.actionButton == kBtnShot) {
-                PlayerCommand c = default_command();
+                PlayerCommand c;
+                default_command(c);
                 c.desiredFunctionType = kFtShot;
                 c.useDesiredMovement = false;
                 c.useDesiredLookAt = false;
@@ -1434,7 +1460,8 @@ CB_HDNI bool human_request_command(const Sim &s, int player, CommandQueue &q) {
     } else if (hc.actionMode == 1) {
         if (btn[hc.actionButton]) {
             if (hc.actionButton == kBtnSliding) {
-                PlayerCommand c = default_command();
+                PlayerCommand c;
+                default_command(c);
                 c.desiredFunctionType = kFtSliding;
                 c.useDesiredMovement = true;
                 c.desiredDirection = ctl.inputDirection;

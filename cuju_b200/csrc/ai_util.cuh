@@ -458,9 +458,12 @@ CB_HD bool dynamic_player_selection(const Match &w) {
     return !((l == sc.leftAgents || sc.leftAgents == 0) && (r == sc.rightAgents || sc.rightAgents == 0));
 }
 
-// The `n` closest active players of a team (ties keep state order); distances in parallel.
-CB_HDNI PlayerList closest_players(const Sim &s, int teamID, const Vec3 &pos, bool onlyAI, unsigned int n = 3,
-                                   bool onlySelectable = false) {
+// The `n` closest active players of a team into `r` (ties keep state order); distances in
+// parallel. The list goes out through a reference: a list returned by value from a call that is
+// not inlined, into a list declared inside a loop, was seen to share its stack slot with a live
+// list of the caller in the sm_100a build.
+CB_HDNI void closest_players(PlayerList &r, const Sim &s, int teamID, const Vec3 &pos, bool onlyAI,
+                             unsigned int n = 3, bool onlySelectable = false) {
     const Match &w = s.w;
     float sd[kPlayers];
     int sp[kPlayers], count = 0;
@@ -486,9 +489,8 @@ CB_HDNI PlayerList closest_players(const Sim &s, int teamID, const Vec3 &pos, bo
         sd[slot] = d;
         sp[slot] = p;
     });
-    PlayerList r;
+    r.count = 0;
     for (unsigned int i = 0; i < n && (int)i < count; i++) r.push(sp[i]);
-    return r;
 }
 
 CB_HDNI int best_switch_target(const Sim &s, int teamID) {
@@ -505,7 +507,8 @@ CB_HDNI int best_switch_target(const Sim &s, int teamID) {
     ob = clampf_((float)((double)(ob - 0.5f) * 2.0 + 0.5), 0.0f, 1.0f);
     ob = clampf_(lm::lm_powf(ob, 1.5f), 0.0f, 1.0f);
     Vec3 res = def * (1.0f - ob) + off * ob;
-    PlayerList tp = closest_players(s, teamID, res, true, 8);
+    PlayerList tp;
+    closest_players(tp, s, teamID, res, true, 8);
     PlayerList kept;
     for (int i = 0; i < tp.count; i++)
         if (formation(s, tp[i]).role != kRoleGK) kept.push(tp[i]);

@@ -252,8 +252,21 @@ public:
             s.rightAgents = bundles[s.bundle].rightAgents;
         }
         if (!estimate) check(cudaMemcpy(b.slots, hostSlots.data(), sizeof(EnvSlot) * c.count, cudaMemcpyHostToDevice), "slots");
+        if (!estimate) reserve_stack();
         started.assign(c.count, false);
         unstarted = c.count;
+    }
+
+    // The kernels' call chains are deep (AI, selection, physics): the per-thread stack is set to
+    // twice what the compiler reports for the deepest kernel, so no call chain can outgrow it.
+    void reserve_stack() {
+        size_t local = 0;
+        int regs = 0;
+        check(kernel_attributes(&local, &regs), "kernel attributes");
+        size_t current = 0;
+        check(cudaDeviceGetLimit(&current, cudaLimitStackSize), "stack limit");
+        const size_t want = (2 * local + 1023) & ~(size_t)1023;
+        if (current < want) check(cudaDeviceSetLimit(cudaLimitStackSize, want), "stack limit");
     }
 
     const AssetVariant &variant(int v) const { return bundles[v / 4].variants[v % 4]; }
@@ -660,6 +673,23 @@ const char *cuju_environment_scenario(void *env, int bundle) {
     if (bundle < 0 || bundle >= (int)e->bundles.size()) return nullptr;
     return e->bundles[bundle].scenario.c_str();
 }
+// No reference counterpart: the kernels' per-thread local memory and registers and the current
+// per-thread stack limit, for diagnosis and the memory estimate.
+int cuju_b200_kernel_info(unsigned long long *out) {
+    try {
+        size_t local = 0, stack = 0;
+        int regs = 0;
+        cb::host::check(cb::kernel_attributes(&local, &regs), "kernel attributes");
+        cb::host::check(cudaDeviceGetLimit(&stack, cudaLimitStackSize), "stack limit");
+        out[0] = local;
+        out[1] = (unsigned long long)regs;
+        out[2] = stack;
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
+}
+
 int cuju_state_layout(void) {
     lastError = "state layouts are not available in this backend";
     return -1;

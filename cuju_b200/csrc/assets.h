@@ -498,7 +498,8 @@ inline void setup_agents(Match &w, const StaticData &sd, int l, int r, const std
     for (int t = 0; t < 2; t++) {
         if (agents[t] == 0) continue;
         const Vec3 ball = ball_predict(m.ball, 0).flat();
-        PlayerList ps = closest_players(s, t, ball, true, (unsigned int)agents[t], true);
+        PlayerList ps;
+        closest_players(ps, s, t, ball, true, (unsigned int)agents[t], true);
         if (ps.count == 0) continue;
         team_by_id(w, t).mainSelectedPlayer = ps[0];
         std::sort(ps.el, ps.el + ps.count, [&](int a, int b) { return sd.stableID[a] < sd.stableID[b]; });

@@ -54,10 +54,10 @@ CB_HD void bounce_off(Vec3 &np, const Vec3 &rel, const Vec3 &post, const Vec3 &f
 // Fills `predictions` in 10 ms steps (entry k: after 10k ms) and returns the next tick's momentum
 // and spin. When the first step lands where the last tick predicted, the previous predictions are
 // shifted down instead (at most `validPredictions` ticks in a row).
-CB_HDNI BallMotion ball_predict_path(Ball &ball, bool ballIsInGoal) {
+CB_HDNI void ball_predict_path(Ball &ball, bool ballIsInGoal, BallMotion &out) {
     const float bounce = 0.62f, linearBounce = 0.06f, drag = 0.015f, friction = 0.04f,
                 linearFriction = 1.6f, gravity = -9.81f, grassHeight = 0.025f, dt = 0.01f;
-    BallMotion out;
+    out = BallMotion{};
     Vec3 np = ball.positionBuffer;
     Quat nextOrientation = ball.orientationBuffer;
     Vec3 mom = ball.momentum;
@@ -224,7 +224,6 @@ CB_HDNI BallMotion ball_predict_path(Ball &ball, bool ballIsInGoal) {
         ball.predictions[t / 10] = np;
         first = false;
     }
-    return out;
 }
 
 struct TimeNeeded {

@@ -16,9 +16,11 @@ CB_HDNI bool check_ball_collisions(const Sim &s) {
     Match &w = s.w;
     MatchState &m = w.m;
     if (m.actualTime_ms <= (uint64_t)(uint32_t)(m.lastBodyBallCollisionTime_ms + 150)) return true;
-    PlayerList players = active_players(w, w.firstTeamID());
+    PlayerList players;
+    active_players(players, w, w.firstTeamID());
     {
-        PlayerList second = active_players(w, 1 - w.firstTeamID());
+        PlayerList second;
+        active_players(second, w, 1 - w.firstTeamID());
         for (int i = 0; i < second.count; i++) players.push(second[i]);
     }
     Vec3 bounce;
@@ -359,9 +361,11 @@ CB_HDNI void check_humanoid_collision(const Sim &s, int a, int b, BounceList &ab
 
 CB_HDNI bool check_humanoid_collisions(const Sim &s) {
     Match &w = s.w;
-    PlayerList players = active_players(w, w.firstTeamID());
+    PlayerList players;
+    active_players(players, w, w.firstTeamID());
     {
-        PlayerList second = active_players(w, 1 - w.firstTeamID());
+        PlayerList second;
+        active_players(second, w, 1 - w.firstTeamID());
         for (int i = 0; i < second.count; i++) players.push(second[i]);
     }
     BounceList bl[kPlayers];

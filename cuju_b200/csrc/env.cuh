@@ -295,7 +295,8 @@ CB_HDNI void environment_get_state(Match &w, const Context &ctx, Observation &o)
         const int teamID = k == 0 ? first : 1 - first;
         TeamObs &to = o.team[teamID];
         const Team &team = team_by_id(w, teamID);
-        PlayerList ps = all_players(w, teamID);
+        PlayerList ps;
+        all_players(ps, w, teamID);
         for (int i = 0; i < ps.count; i++) {
             const int p = ps[i];
             const Player &pl = m.players[p];

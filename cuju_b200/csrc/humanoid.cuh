@@ -166,8 +166,9 @@ CB_HDNI void team_gamers_select_anyone(const Sim &s, int teamID) {
 
 // ---------------------------------------------------------------------------------------------
 // Commands.
-CB_HDNI PlayerCommand default_command() {
-    PlayerCommand c;
+// Commands are built through a reference, not returned by value: aggregates returned by value from
+// inlined calls were seen to lose their stack slot in the sm_100a build.
+CB_HD void default_command(PlayerCommand &c) {
     memset(&c, 0, sizeof(c));
     c.desiredFunctionType = kFtMovement;
     c.useDesiredMovement = false;
@@ -186,10 +187,9 @@ CB_HDNI PlayerCommand default_command() {
     c.modifier = 0;
     c.touchInfo.targetPlayer = -1;
     c.touchInfo.forcedTargetPlayer = -1;
-    return c;
 }
-CB_HD PlayerCommand trip_command(const Humanoid &h, const Vec3 &trip, int tripType) {
-    PlayerCommand c = default_command();
+CB_HD void trip_command(PlayerCommand &c, const Humanoid &h, const Vec3 &trip, int tripType) {
+    default_command(c);
     c.desiredFunctionType = kFtTrip;
     c.useDesiredMovement = false;
     c.useDesiredTripDirection = true;
@@ -197,7 +197,6 @@ CB_HD PlayerCommand trip_command(const Humanoid &h, const Vec3 &trip, int tripTy
     c.desiredVelocityFloat = h.spatial.floatVelocity;
     c.useTripType = true;
     c.tripType = tripType;
-    return c;
 }
 CB_HD bool queue_push(const Sim &s, CommandQueue &q, const PlayerCommand &c) {
     if (q.count >= 16) return s.fail(kStatusOverflow);
@@ -205,25 +204,29 @@ CB_HD bool queue_push(const Sim &s, CommandQueue &q, const PlayerCommand &c) {
     return true;
 }
 CB_HD void add_trip_commands(const Sim &s, const Humanoid &h, CommandQueue &q, int tripType) {
+    PlayerCommand c;
     if (tripType == 1) {
-        queue_push(s, q, trip_command(h, h.tripDirection, tripType));
+        trip_command(c, h, h.tripDirection, tripType);
+        queue_push(s, q, c);
     } else {
         int other = 3;
         if (tripType == 3) other = 2;
-        queue_push(s, q, trip_command(h, h.tripDirection, tripType));
-        queue_push(s, q, trip_command(h, h.tripDirection, other));
-        queue_push(s, q, trip_command(h, h.tripDirection, 1));
+        trip_command(c, h, h.tripDirection, tripType);
+        queue_push(s, q, c);
+        trip_command(c, h, h.tripDirection, other);
+        queue_push(s, q, c);
+        trip_command(c, h, h.tripDirection, 1);
+        queue_push(s, q, c);
     }
 }
-CB_HD PlayerCommand basic_movement_command(const Humanoid &h, float vel) {
-    PlayerCommand c = default_command();
+CB_HD void basic_movement_command(PlayerCommand &c, const Humanoid &h, float vel) {
+    default_command(c);
     c.desiredFunctionType = kFtMovement;
     c.useDesiredMovement = true;
     c.useDesiredLookAt = true;
     c.desiredDirection = h.spatial.directionVector;
     c.desiredVelocityFloat = vel;
     c.desiredLookAt = h.spatial.position + c.desiredDirection * 10.0f;
-    return c;
 }
 
 CB_HDNI bool player_request_command(const Sim &s, int p, CommandQueue &q);  // ai_ctrl.cuh
@@ -287,7 +290,9 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
         if (h.interruptAnim == kIntTrip && h.tripType != 0) {
             add_trip_commands(s, h, q, h.tripType);
             h.tripType = 0;
-            queue_push(s, q, basic_movement_command(h, h.spatial.floatVelocity));
+            PlayerCommand bmc;
+            basic_movement_command(bmc, h, h.spatial.floatVelocity);
+            queue_push(s, q, bmc);
         } else {
             q.count = 0;
             if (!player_request_command(s, p, q)) return false;

@@ -38,7 +38,7 @@ CB_HDNI bool player_process(const Sim &s, int p) {
             d * 0.00003f * (2.0f - stamina) * (1.0f / s.ctx.staticData->matchDurationFactor);
         pl.base.fatigueFactorInverse = clampf_(pl.base.fatigueFactorInverse, 0.01f, 1.0f);
     }
-    if (pl.cards > 1 && pl.cardEffectiveTime_ms <= m.actualTime_ms && active_players(w, w.playerTeamID[p]).count > 1)
+    if (pl.cards > 1 && pl.cardEffectiveTime_ms <= m.actualTime_ms && active_count(w, w.playerTeamID[p]) > 1)
         return player_send_off(s, p);
     return true;
 }
@@ -138,7 +138,8 @@ CB_HDNI void push_mental_image(Match &w) {
     im.maxMovementDeviation = kWalkVel;
     for (int slot = 0; slot < 2; slot++) {
         const int teamID = slot == 0 ? w.firstTeamID() : 1 - w.firstTeamID();
-        PlayerList ps = active_players(w, teamID);
+        PlayerList ps;
+        active_players(ps, w, teamID);
         for (int i = 0; i < ps.count; i++) {
             const int p = ps[i];
             const SpatialState &sp = hum(w, p).spatial;
@@ -386,12 +387,14 @@ CB_HDNI void match_prepare_put_buffers(const Sim &s) {
     const int first = w.firstTeamID(), second = 1 - first;
     mirror_match(w, false, false, first == 1);
     {
-        PlayerList ps = active_players(w, first);
+        PlayerList ps;
+        active_players(ps, w, first);
         par_for(ps.count, [&](int i) { player_prepare_put_buffers(s, ps[i]); });
     }
     mirror_match(w, false, false, true);
     {
-        PlayerList ps = active_players(w, second);
+        PlayerList ps;
+        active_players(ps, w, second);
         par_for(ps.count, [&](int i) { player_prepare_put_buffers(s, ps[i]); });
     }
     mirror_match(w, false, false, first == 0);
@@ -405,7 +408,8 @@ CB_HDNI bool match_fetch_put_buffers(const Sim &s) {
     int16_t hidx[kPutHumanoids];
     int n = 0;
     for (int t = 0; t < 2; t++) {
-        PlayerList ps = active_players(w, t == 0 ? first : second);
+        PlayerList ps;
+        active_players(ps, w, t == 0 ? first : second);
         for (int i = 0; i < ps.count; i++) hidx[n++] = (int16_t)ps[i];
     }
     for (int o = 0; o < 3; o++) hidx[n++] = (int16_t)(w.m.playerCount + o);

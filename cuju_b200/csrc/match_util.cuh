@@ -628,17 +628,27 @@ CB_HDNI void update_possession_stats(Match &w, const StaticData &sd, int p) {
 // ---------------------------------------------------------------------------------------------
 // Team side, active players, passes and shots.
 CB_HD int team_side(const Match &w, int teamID) { return w.flags.teamSide[teamID]; }
-CB_HD PlayerList active_players(const Match &w, int teamID) {
-    PlayerList l;
+// Team rosters go out through a reference: lists returned by value were seen to lose their stack
+// slot to later lists of the caller in the sm_100a build.
+CB_HD void active_players(PlayerList &l, const Match &w, int teamID) {
+    l.count = 0;
     for (int p = 0; p < w.m.playerCount; p++)
         if (w.playerTeamID[p] == teamID && w.m.players[p].base.isActive) l.push(p);
-    return l;
 }
-CB_HD PlayerList all_players(const Match &w, int teamID) {
-    PlayerList l;
+CB_HD void all_players(PlayerList &l, const Match &w, int teamID) {
+    l.count = 0;
     for (int p = 0; p < w.m.playerCount; p++)
         if (w.playerTeamID[p] == teamID) l.push(p);
-    return l;
+}
+CB_HD int active_count(const Match &w, int teamID) {
+    int n = 0;
+    for (int p = 0; p < w.m.playerCount; p++) n += w.playerTeamID[p] == teamID && w.m.players[p].base.isActive;
+    return n;
+}
+CB_HD int team_count(const Match &w, int teamID) {
+    int n = 0;
+    for (int p = 0; p < w.m.playerCount; p++) n += w.playerTeamID[p] == teamID;
+    return n;
 }
 CB_HDNI void auto_pass(int passType, const Vec3 &v, Vec3 &dir, float &power) {
     float heightOffset = 0.11f, powerFactor = 1.8f, distExp = 1.4f;
@@ -665,7 +675,8 @@ CB_HDNI void get_pass(const Match &w, int p, int passType, const Vec3 &inputDir,
     Vec3 pp = sp.position + sp.movement.normalized(Vec3(0)) * 0.2f;
     if (ca.touchFrame != -1) pp = ca.touchPosition.flat();
     Vec3 manualTarget = pp + inputDir * clampf_(inputPower * 60.0f, 1.0f, 100.0f);
-    PlayerList players = active_players(w, teamID);
+    PlayerList players;
+    active_players(players, w, teamID);
     if (players.count < 2) {
         outDir = sp.directionVector;
         outPower = 1.0f;

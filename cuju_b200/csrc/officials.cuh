@@ -154,7 +154,8 @@ CB_HDNI void referee_request_command(const Sim &s, int official, CommandQueue &q
             const Vec3 offender = hum(w, ref.foul.foulPlayer).spatial.position;
             Vec3 des = offender + (pos - offender).normalized(Vec3(0)) * (float)2.0;
             if ((double)(pos - des).length() > 2.0) {
-                PlayerCommand c = default_command();
+                PlayerCommand c;
+                default_command(c);
                 c.desiredFunctionType = kFtMovement;
                 c.useDesiredMovement = true;
                 c.useDesiredLookAt = true;
@@ -163,14 +164,16 @@ CB_HDNI void referee_request_command(const Sim &s, int official, CommandQueue &q
                 c.desiredLookAt = offender;
                 queue_push(s, q, c);
             } else {
-                PlayerCommand c = default_command();
+                PlayerCommand c;
+                default_command(c);
                 c.desiredFunctionType = kFtSpecial;
                 c.useDesiredMovement = false;
                 c.useDesiredLookAt = false;
                 c.useSpecialVar1 = true;
                 c.specialVar1 = 3;
                 queue_push(s, q, c);
-                PlayerCommand f = default_command();
+                PlayerCommand f;
+                default_command(f);
                 f.desiredFunctionType = kFtMovement;
                 f.useDesiredMovement = true;
                 f.useDesiredLookAt = true;
@@ -180,7 +183,8 @@ CB_HDNI void referee_request_command(const Sim &s, int official, CommandQueue &q
                 queue_push(s, q, f);
             }
         } else {
-            PlayerCommand c = default_command();
+            PlayerCommand c;
+            default_command(c);
             c.desiredFunctionType = kFtMovement;
             c.useDesiredMovement = true;
             c.useDesiredLookAt = true;
@@ -204,7 +208,8 @@ CB_HDNI void referee_request_command(const Sim &s, int official, CommandQueue &q
             }
             const int teams[2] = {w.firstTeamID(), 1 - w.firstTeamID()};
             for (int t = 0; t < 2; t++) {
-                PlayerList ap = active_players(w, teams[t]);
+                PlayerList ap;
+                active_players(ap, w, teams[t]);
                 for (int i = 0; i < ap.count; i++) {
                     const SpatialState &ps = hum(w, ap[i]).spatial;
                     ForceSpot spx;
@@ -223,7 +228,8 @@ CB_HDNI void referee_request_command(const Sim &s, int official, CommandQueue &q
             queue_push(s, q, c);
         }
     } else {
-        PlayerCommand c = default_command();
+        PlayerCommand c;
+        default_command(c);
         c.desiredFunctionType = kFtMovement;
         c.useDesiredMovement = true;
         c.useDesiredLookAt = true;
@@ -262,7 +268,9 @@ CB_HDNI bool official_process(const Sim &s, int official) {
         if (h.interruptAnim == kIntTrip && h.tripType != 0) {
             add_trip_commands(s, h, q, h.tripType);
             h.tripType = 0;
-            queue_push(s, q, basic_movement_command(h, h.spatial.floatVelocity));
+            PlayerCommand bmc;
+            basic_movement_command(bmc, h, h.spatial.floatVelocity);
+            queue_push(s, q, bmc);
         } else {
             referee_request_command(s, official, q);
         }

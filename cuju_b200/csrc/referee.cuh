@@ -247,7 +247,7 @@ CB_HDNI bool referee_ball_touched(const Sim &s) {
     if (!w.scenario.offsides) return true;
     const int ltt = m.lastTouchTeamID;
     if (ltt == -1) return true;
-    if (m.inPlay && !m.inSetPiece && b.active == false && active_players(w, 1 - ltt).count > 1) {
+    if (m.inPlay && !m.inSetPiece && b.active == false && active_count(w, 1 - ltt) > 1) {
         const int owner = match_last_touch_player(w);
         for (int i = 0; i < ref.offsidePlayers.count; i++) {
             if (ref.offsidePlayers.el[i] != owner) continue;
@@ -265,7 +265,8 @@ CB_HDNI bool referee_ball_touched(const Sim &s) {
                                            b.desiredSetPiece != kGmCorner))) {
         // A fresh mental image: the defenders and the ball as they are this tick.
         ImageList im;
-        PlayerList def = active_players(w, 1 - ltt);
+        PlayerList def;
+        active_players(def, w, 1 - ltt);
         for (int i = 0; i < def.count; i++) {
             const SpatialState &sp = hum(w, def[i]).spatial;
             im.push(ImagePos{sp.position, sp.movement, m.players[def[i]].dynamicFormationEntry.role});
@@ -273,7 +274,8 @@ CB_HDNI bool referee_ball_touched(const Sim &s) {
         const int side = team_side(w, ltt);
         float line = offside_line_from_images(im, ball_predict(m.ball, 0), team_side(w, 1 - ltt), 0);
         const int tlp = team_by_id(w, ltt).lastTouchPlayer;
-        PlayerList att = active_players(w, ltt);
+        PlayerList att;
+        active_players(att, w, ltt);
         for (int i = 0; i < att.count; i++) {
             const int p = att[i];
             if (p == tlp) continue;

@@ -216,7 +216,8 @@ CB_HDNI bool team_reset_situation(const Sim &s, int teamID, const Vec3 &focus) {
     t.teamPossessionAmount = 1.0f;
     t.fadingTeamPossessionAmount = 1.0f;
     t.lastTouchPlayer = -1;
-    PlayerList ps = all_players(w, teamID);
+    PlayerList ps;
+    all_players(ps, w, teamID);
     if (ps.count == 0) return s.fail(kStatusUnsupported);
     t.designatedTeamPossessionPlayer = ps[0];
     for (int i = 0; i < ps.count; i++)
@@ -274,7 +275,8 @@ CB_HDNI bool team_ai_prepare_set_piece(const Sim &s, int teamID, int setPiece, i
     auto reset_pos = [&](int p, const Vec3 &pos, const Vec3 &focus) { return humanoid_reset_position(s, p, pos, focus); };
     ai.setPieceType = setPiece;
     if (setPiece == kGmNormal) return true;
-    PlayerList players = active_players(w, teamID);
+    PlayerList players;
+    active_players(players, w, teamID);
     for (int i = 0; i < players.count;) {
         Vec3 focus = flat_ball();
         if (formation(s, players[i]).role == kRoleGK) {
@@ -307,7 +309,8 @@ CB_HDNI bool team_ai_prepare_set_piece(const Sim &s, int teamID, int setPiece, i
                 }
                 if (!reset_pos(players[i], bp, flat_ball())) return false;
                 if (taker) {
-                    PlayerList r = closest_players(s, teamID, Vec3(0), false, 2);
+                    PlayerList r;
+                    closest_players(r, s, teamID, Vec3(0), false, 2);
                     for (int k = 0; k < r.count; k++)
                         if (!reset_pos(r[k], Vec3(0, F((double)k * 1.4 * dside), 0), flat_ball())) return false;
                 }
@@ -415,7 +418,8 @@ CB_HDNI bool team_ai_prepare_set_piece(const Sim &s, int teamID, int setPiece, i
                 if (!reset_pos(players[i], bp, flat_ball())) return false;
             }
             if (!taker && (double)(flat_ball() - Vec3(side * kPitchHalfL, 0, 0)).length() < 40.0) {
-                PlayerList r = closest_players(s, teamID, flat_ball(), false, 3);
+                PlayerList r;
+                closest_players(r, s, teamID, flat_ball(), false, 3);
                 for (int k = 0; k < r.count; k++) {
                     Vec3 tg = (Vec3(side * kPitchHalfL, 0, 0) - flat_ball()).normalized(Vec3(0));
                     tg += Vec3(0, F(1.0 - (double)k), 0) * F(0.07);
@@ -464,13 +468,15 @@ CB_HDNI bool team_ai_prepare_set_piece(const Sim &s, int teamID, int setPiece, i
     }
 
     if (setPiece == kGmKickOff) {
-        PlayerList fps = all_players(w, teamID);
-        PlayerList tps = all_players(w, teamID);
+        PlayerList fps;
+        all_players(fps, w, teamID);
+        PlayerList tps;
+        all_players(tps, w, teamID);
         // After the start, a kickoff to the team that did not own the ball at the start swaps the
         // start positions of equal-sized teams.
-        if (m.matchTime_ms > 0 && all_players(w, otherTeamID).count == fps.count &&
+        if (m.matchTime_ms > 0 && team_count(w, otherTeamID) == fps.count &&
             (left_team_owns_ball(w) ^ (kickoffTakerTeamID == 0)))
-            fps = all_players(w, otherTeamID);
+            all_players(fps, w, otherTeamID);
         for (int i = 0; i < fps.count; i++) {
             if (!m.players[tps[i]].base.isActive) continue;
             Vec3 bp = formation(s, fps[i]).startPosition * Vec3(-side * kPitchHalfL, -side * kPitchHalfW, 0);
@@ -480,7 +486,8 @@ CB_HDNI bool team_ai_prepare_set_piece(const Sim &s, int teamID, int setPiece, i
 
     if (taker) {
         Vec3 b = flat_ball();
-        PlayerList cl = closest_players(s, teamID, flat_ball(), false, 2);
+        PlayerList cl;
+        closest_players(cl, s, teamID, flat_ball(), false, 2);
         if (cl.count == 0) return s.fail(kStatusUnsupported);
         ai.taker = cl[0];
         if (setPiece == kGmKickOff) {

@@ -117,7 +117,8 @@ CB_HDNI bool team_ai_process(const Sim &s, int teamID) {
     if (lineX * side - slack > deepest * side) deepest = lineX - slack * side;
     ai.offsideTrapX = deepest;
 
-    PlayerList players = active_players(w, 1 - teamID);
+    PlayerList players;
+    active_players(players, w, 1 - teamID);
     Vec3 mdp = Vec3((float)(((double)kPitchHalfL - 2.0) * side), 0, 0);
     mdp = mdp * 0.8f + ball_predict(m.ball, 100).flat() * 0.2f;
     if (players.count > 16) return s.fail(kStatusUnsupported);
@@ -153,7 +154,8 @@ CB_HDNI bool team_ai_process(const Sim &s, int teamID) {
                 float d = (posOf(runner) - posOf(team.designatedTeamPossessionPlayer)).length();
                 float dr = lm::lm_powf(1.0f - nclamp(d, 0, 40), 0.5f);
                 Vec3 spot = posOf(runner) * Vec3(1.0f, 0.8f, 0.0f) + Vec3(side * 10.0f, 0, 0);
-                PlayerList opps = closest_players(s, 1 - teamID, spot, false, 4);
+                PlayerList opps;
+                closest_players(opps, s, 1 - teamID, spot, false, 4);
                 float dens = 1.0f;
                 for (int i = 0; i < opps.count; i++) {
                     float od = (posOf(opps[i]) - spot).length();
@@ -312,7 +314,8 @@ CB_HDNI int hungarian_solve(int *cost, int size, int *colOfRow_out) {
 /// team_ai.h:385 (TeamCalculateDynamicRoles).
 CB_HDNI bool team_dynamic_roles(const Sim &s, int teamID) {
     Match &w = s.w;
-    PlayerList all = active_players(w, teamID);
+    PlayerList all;
+    active_players(all, w, teamID);
     int players[kTeamPlayers];
     int n = 0;
     if (all.count > 0) {
@@ -406,7 +409,8 @@ CB_HDNI float marking_quality(const Match &w, int teamID, int player, int oppone
 CB_HDNI void team_man_marking(const Sim &s, int teamID) {
     Match &w = s.w;
     const TeamAIState &ai = team_by_id(w, teamID).ai;
-    PlayerList players = active_players(w, teamID);
+    PlayerList players;
+    active_players(players, w, teamID);
     for (int i = 0; i < players.count; i++) w.m.players[players[i]].manMarking = -1;
     const int marked = std_min((int)ai.opponentInfo.count, 3);
     for (int rank = 0; rank < marked; rank++) {

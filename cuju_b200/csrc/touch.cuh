@@ -11,13 +11,15 @@ namespace cb {
 
 CB_HD void ball_recalc(Match &w) {
     ball_materialize(w.m.ball);
-    ball_predict_path(w.m.ball, w.m.ballIsInGoal);
+    BallMotion unused;
+    ball_predict_path(w.m.ball, w.m.ballIsInGoal, unused);
 }
 
 // One tick of the ball: predict, advance one step, append the position history (401 entries).
 CB_HDNI void ball_process(Ball &b, bool inGoal) {
     ball_materialize(b);
-    BallMotion bm = ball_predict_path(b, inGoal);
+    BallMotion bm;
+    ball_predict_path(b, inGoal, bm);
     b.momentum = bm.momentum;
     b.rotationPerMs = bm.rotationPerMs;
     b.positionBuffer = predict_at(b.predictions, 10);

@@ -89,6 +89,9 @@ void *cuju_environment_buffer(void *environment, const char *name);
 /* environment_api.h:470 */ int cuju_environment_episode(void *environment, int index, long long *values,
                                                          float *difficulty);
 /* environment_api.h:519 */ const char *cuju_environment_scenario(void *environment, int bundle);
+/* No reference counterpart: out[0] the kernels' per-thread local memory in bytes, out[1] their
+ * registers per thread, out[2] the current per-thread stack limit. */
+int cuju_b200_kernel_info(unsigned long long *out);
 /* src/state_api.h (state field layout and gather); this backend reports them unavailable */
 int cuju_state_layout(void);
 int cuju_state_gather(void);
