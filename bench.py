@@ -34,6 +34,9 @@ DIFFICULTY = (0.2, 0.2)
 ENVS_PER_GPU = 16384
 METRIC = 'env steps/sec, 11v11 at 1/2/4/8 B200 vs host-CPU path; % HBM roofline'
 STATE_BYTES = 106914  # serialized GRF state of 11_vs_11 with one left agent (measured by get_state)
+# DRAM bytes (read + write) per env-step of step_kernel: 14.173 GB over one 4,096-environment launch
+# (ncu --set full, dram__bytes_read.sum + dram__bytes_write.sum).
+TRAFFIC_PER_ENV_STEP = 14.173e9 / 4096
 
 
 def bytes_per_env_step(agents: int = 1, stack: int = 1, state: int = STATE_BYTES) -> int:
@@ -253,9 +256,11 @@ def run_b200(args) -> None:
                     'd2h_bytes_per_step': envs * agents * 115 * 4 + envs * agents * 4 + envs},
             'gpu_launches': args.steps,
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s',
-                         'frac': achieved / peak, 'traffic': None,
+                         'frac': achieved / peak, 'traffic': TRAFFIC_PER_ENV_STEP * envs / 1e9,
                          'note': f'algorithmic {per_step} B per env-step x {envs} env-steps per launch over the '
-                                 f'mean CUDA-event time of a step launch; peak {peak_kind}'},
+                                 f'mean CUDA-event time of a step launch; peak {peak_kind} (of measured); traffic '
+                                 'in GB per launch, DRAM read+write of one ncu capture at 4,096 environments '
+                                 'scaled by the environments processed'},
             'clocks': clock,
         }
         if args.cpu_baseline:

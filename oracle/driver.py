@@ -32,7 +32,7 @@ class OracleBatch:
 
     def __init__(self, bundle_paths, agent_counts, environment_count, seed, animations, threads=1,
                  representation=2, checkpoints=False, stack=1, assignment=None, difficulty=None,
-                 auto_reset=True, ticks_per_step=10):
+                 auto_reset=True, ticks_per_step=10, first_index=0):
         if not os.path.isfile(LIBRARY):
             raise RuntimeError(f'the oracle library is missing at {LIBRARY}; run make -C oracle')
         native = _configuration_type()
@@ -50,7 +50,7 @@ class OracleBatch:
             action_set=0, observation=representation, checkpoints=int(checkpoints), numpy_legacy=1,
             auto_reset=int(auto_reset), threads=threads, ticks_per_step=ticks_per_step, smm_width=96, smm_height=72,
             stack=stack, fixed_seeds=None, agent_counts=ctypes.cast(counts, ctypes.c_void_p),
-            episode_number=0, first_index=0, allocate=None, release=None, allocator_context=None,
+            episode_number=0, first_index=first_index, allocate=None, release=None, allocator_context=None,
             pin_threads=0, numa=0, page_aligned=0)
         self.handle = self.lib.cuju_environment_create(ctypes.byref(config))
         if not self.handle:
