@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -384,6 +385,46 @@ public:
         if (synchronize) sync(stream);
         else if (!onDevice) check(cudaStreamSynchronize(stream), "host actions");
     }
+    // The step with device-resident actions and the fixed sort scratch of kernels.cu in place of
+    // the batch's own: no allocation of any kind. Returns null, or the reason for refusing.
+    const char *step_static(const int32_t *actions, cudaStream_t stream, char *message, size_t size) {
+        if (unstarted > 0) return "expected a reset of the batch before its first step";
+        if (b.count > kStaticScratchEnvironments) {
+            snprintf(message, size, "expected at most %d environments for the static-scratch step, found %d",
+                     kStaticScratchEnvironments, b.count);
+            return message;
+        }
+        if (!actions) return "expected device actions";
+        int device = -1;
+        if (cudaGetDevice(&device) != cudaSuccess) return "no current CUDA device";
+        // A failed attribute query leaves a non-sticky error behind; it is cleared so that a later
+        // launch check does not report it.
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, actions) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return "expected actions in device memory of the current device";
+        }
+        if ((a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) || a.device != device)
+            return "expected actions in device memory of the current device";
+        cudaPointerAttributes own{};
+        if (cudaPointerGetAttributes(&own, b.status) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return "expected the batch's device to be the current device";
+        }
+        if (own.device != device) return "expected the batch's device to be the current device";
+        WarpScratch *scratch = nullptr;
+        cudaError_t rc = static_scratch_address(&scratch);
+        if (rc == cudaSuccess) {
+            Batch view = b;
+            view.scratch = scratch;
+            rc = launch_step(view, actions, stream);
+        }
+        if (rc != cudaSuccess) {
+            snprintf(message, size, "static-scratch step: %s", cudaGetErrorString(rc));
+            return message;
+        }
+        return nullptr;
+    }
     void reset_done(cudaStream_t stream) {
         check_started();
         check(launch_reset(b, b.done, nullptr, nullptr, stream), "reset launch");
@@ -569,6 +610,14 @@ int cuju_environment_step(void *env, const int *actions, int on_device, void *st
     } catch (const std::exception &e) {
         return fail(e);
     }
+}
+// No reference counterpart: see include/cuju_b200.h. The success path allocates nothing.
+int cuju_b200_environment_step_static(void *env, const int *actions, void *stream) {
+    thread_local char message[160];
+    const char *why = static_cast<BatchEnv *>(env)->step_static(actions, as_stream(stream), message, sizeof message);
+    if (!why) return 0;
+    lastError.assign(why);
+    return -1;
 }
 int cuju_environment_step_async(void *env, const int *actions, int on_device, void *stream) {
     try {

@@ -4,6 +4,8 @@
 // launches them through the wrappers at the end, on the caller's stream.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "kernels.h"
 
 namespace cb {
@@ -58,6 +60,28 @@ cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t str
     output_kernel<<<grid_for(b.count), kThreadsPerBlock, 0, stream>>>(b, mask);
     return cudaGetLastError();
 }
+// The static-scratch step's sort scratch. Nothing in it needs to start at zero: every sort writes
+// the keys and positions it reads.
+static __device__ __align__(256) WarpScratch staticScratch[kStaticScratchEnvironments];
+
+cudaError_t static_scratch_address(WarpScratch **out) {
+    static std::atomic<WarpScratch *> cached[kStaticScratchDevices];
+    int device = -1;
+    cudaError_t rc = cudaGetDevice(&device);
+    if (rc != cudaSuccess) return rc;
+    if (device < 0 || device >= kStaticScratchDevices) return cudaErrorInvalidDevice;
+    WarpScratch *p = cached[device].load(std::memory_order_acquire);
+    if (!p) {
+        void *address = nullptr;
+        rc = cudaGetSymbolAddress(&address, staticScratch);
+        if (rc != cudaSuccess) return rc;
+        p = static_cast<WarpScratch *>(address);
+        cached[device].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return cudaSuccess;
+}
+
 cudaError_t kernel_attributes(size_t *localBytes, int *registers) {
     cudaFuncAttributes a;
     cudaError_t rc = cudaFuncGetAttributes(&a, step_kernel);

@@ -18,4 +18,12 @@ cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t str
 // The largest per-thread local memory and register count of the kernels.
 cudaError_t kernel_attributes(size_t *localBytes, int *registers);
 
+// A fixed sort scratch in device memory (a file-scope array of kernels.cu) for the static-scratch
+// step: room for kStaticScratchEnvironments environments, 32 x 38,912 B = 1.19 MiB per device.
+constexpr int kStaticScratchEnvironments = 32;
+constexpr int kStaticScratchDevices = 64;
+// The array's address on the current device, looked up once per device (cudaGetSymbolAddress
+// with that device current) and cached; allocates nothing.
+cudaError_t static_scratch_address(WarpScratch **out);
+
 }  // namespace cb

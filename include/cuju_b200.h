@@ -92,6 +92,18 @@ void *cuju_environment_buffer(void *environment, const char *name);
 /* No reference counterpart: out[0] the kernels' per-thread local memory in bytes, out[1] their
  * registers per thread, out[2] the current per-thread stack limit. */
 int cuju_b200_kernel_info(unsigned long long *out);
+/* No reference counterpart. One step of a batch of at most 32 environments with actions already in
+ * device memory of the current device, using a fixed 1.19 MiB device scratch array (room for 32
+ * environments' sort keys) in place of the batch's own scratch. The success path allocates
+ * nothing: no cudaMalloc/cudaFree, no host heap, no allocator callback. Asynchronous on `stream`
+ * like cuju_environment_step_async; errors inside the step surface at the next
+ * cuju_environment_synchronize. The first call on a device looks up the array's address with
+ * cudaGetSymbolAddress while that device is current; make it before any stream capture. Nothing
+ * in the array needs to start at zero (every sort writes what it reads). Calls that overlap in
+ * time on one device (any stream, any batch) share the array and race: issue them one at a time.
+ * Returns 0, or -1 with the reason in cuju_last_error (more than 32 environments, host or foreign
+ * actions, a batch not yet reset, a CUDA error). */
+int cuju_b200_environment_step_static(void *environment, const int *actions, void *stream);
 /* src/state_api.h (state field layout and gather); this backend reports them unavailable */
 int cuju_state_layout(void);
 int cuju_state_gather(void);

@@ -17,7 +17,7 @@ ORACLE = os.path.join(ROOT, 'oracle', '_ref', 'libcuju_cpu.so')
 def declared_symbols():
     with open(HEADER, encoding='utf-8') as handle:
         text = handle.read()
-    return sorted(set(re.findall(r'\b(cuju_[a-z_]+)\s*\(', text)))
+    return sorted(set(re.findall(r'\b(cuju_[a-z0-9_]+)\s*\(', text)))
 
 
 def test_header_declares_the_reference_entry_points():
