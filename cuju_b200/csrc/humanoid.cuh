@@ -236,124 +236,78 @@ CB_HD Vec3 current_outgoing_movement(const AnimationState &ca) {
     return (ca.positions[ca.positions.count - 1] - ca.positions[ca.positions.count - 2]) * 100.0f;
 }
 
-// One tick of a player's humanoid.
-CB_HDNI bool humanoid_process(const Sim &s, int p) {
+// The interrupt branch of a humanoid tick (humanoid_process.h): the command request, the
+// animation selection over the queued commands and the new animation's start. Reads and writes
+// only the match, so a whole warp can run it for one environment.
+CB_HDNI bool humanoid_interrupt(const Sim &s, int p) {
+    Humanoid &h = s.w.m.players[p].base.humanoid;
+    AnimationState &ca = h.anim;
+    CommandQueue q;
+    if (h.interruptAnim == kIntTrip && h.tripType != 0) {
+        add_trip_commands(s, h, q, h.tripType);
+        h.tripType = 0;
+        PlayerCommand bmc;
+        basic_movement_command(bmc, h, h.spatial.floatVelocity);
+        queue_push(s, q, bmc);
+    } else {
+        q.count = 0;
+        if (!player_request_command(s, p, q)) return false;
+    }
+    bool found = false, preferPass = false;
+    for (int i = 0; i < q.count; i++) {
+        const PlayerCommand &c = q[i];
+        if (c.desiredFunctionType == kFtShortPass || c.desiredFunctionType == kFtLongPass ||
+            c.desiredFunctionType == kFtHighPass || c.desiredFunctionType == kFtShot)
+            preferPass = true;
+        Selector sel(s, p);
+        int r = sel.select(c, h.interruptAnim, preferPass);
+        if (r == kSelUnsupported) return s.fail(kStatusUnsupported);
+        if (*s.status != kStatusOk) return false;
+        found = r == kSelTrue;
+        if (found) break;
+    }
+    if (h.interruptAnim == kIntSwitch && !found) return s.fail(kStatusUnsupported);
+    if (found) {
+        h.startPosition = h.spatial.position;
+        h.startAngle = h.spatial.angle;
+        {
+            Selector sel(s, p);
+            Vec3 nsp;
+            float nsa;
+            sel.predicted_situation(nsp, nsa);
+            h.nextStartPosition = nsp;
+            set_radian(h.nextStartAngle, nsa);
+        }
+        h.applyBuffer.anim = ca.anim;
+        h.applyBuffer.smooth = true;
+        h.applyBuffer.smoothFactor = (h.interruptAnim == kIntSwitch && h.prevAnimFunctionType == kFtMovement &&
+                                      ca.functionType == kFtMovement)
+                                         ? 0.0f
+                                         : 1.0f;
+        if (ca.functionType == kFtShot) h.applyBuffer.smoothFactor = 0.8f;
+        if (ca.functionType == kFtShortPass || ca.functionType == kFtHighPass) h.applyBuffer.smoothFactor = 0.8f;
+        if (ca.functionType == kFtDeflect || ca.functionType == kFtSliding) h.applyBuffer.smoothFactor = 0.8f;
+        if (ca.functionType == kFtBallControl || ca.functionType == kFtTrap) h.applyBuffer.smoothFactor = 0.8f;
+        float ad = s.D(ca.anim).animDifficultyFactor;
+        if (ad > h.decayingDifficultyFactor) h.decayingDifficultyFactor = ad;
+        if (h.interruptAnim == kIntReQueue && h.prevAnimFunctionType == ca.functionType) h.requeueDelayFrames = 22;
+    }
+    return true;
+}
+
+// The touch part of a humanoid tick (humanoid_process.h): a controlled collision, the touch at the
+// animation's touch frame (trap, control, pass, shot, deflection ...) and the retained ball. Reads
+// and writes only the match, so a whole warp can run it for one environment; `arg` is the player
+// plus 0x10000 when a controlled collision was triggered this tick.
+CB_HDNI bool humanoid_touches(const Sim &s, int arg) {
+    const int p = arg & 0xffff;
+    const bool ctrlColl = (arg & 0x10000) != 0;
     Match &w = s.w;
     Player &pl = w.m.players[p];
     Humanoid &h = pl.base.humanoid;
     AnimationState &ca = h.anim;
     const int teamID = w.playerTeamID[p];
-    const Team &team = team_by_id(w, teamID);
-    const Ball &ball = w.m.ball;
-    const int mi = mental_index(w, h.mentalImageTime);
-    h.decayingPositionOffset *= 0.95f;
-    if ((double)h.decayingPositionOffset.length() < 0.005) h.decayingPositionOffset = Vec3(0);
-    h.decayingDifficultyFactor = clampf_(h.decayingDifficultyFactor - 0.002f, 0.0f, 1.0f);
-    bool teamTouchedLast = w.m.lastTouchTeamID == teamID;
-    h.mentalImageTime = teamTouchedLast ? 0 : reaction_time_ms(s, p);
-    calc_spatial_state(s, h);
-    h.spatial.positionOffsetMovement = Vec3(0);
-    ca.frameNumber++;
-    h.prevAnimFrameNumber++;
-    {
-        const Anim &a = s.A(ca.anim);
-        if (ca.frameNumber == a.frameCount - 1 && h.interruptAnim == kIntNone) h.interruptAnim = kIntSwitch;
-        bool mayRequeue = true;
-        if (mayRequeue && h.interruptAnim != kIntNone) mayRequeue = false;
-        if (mayRequeue) {
-            bool fnp = false;
-            float ad = ((h.spatial.position + h.spatial.movement * 0.1f) - ball_predict(ball, 100).flat()).length();
-            uint64_t second = team_slot(w, teamID) == 1 ? 1 : 0;
-            uint64_t t = w.m.actualTime_ms;
-            if (w.m.designatedPossessionPlayer == p && ad < 3.0f) fnp = ((t + second * 10) % 20) == 0;
-            else if (w.m.designatedPossessionPlayer == p) fnp = ((t + second * 10) % 30) == 0;
-            else if (team.designatedTeamPossessionPlayer == p) fnp = ((t + second * 20) % 40) == 0;
-            else if (ad < 5.0f) fnp = ((t + second * 20) % 50) == 0;
-            else if (ad < 10.0f) fnp = ((t + second * 40) % 80) == 0;
-            if (!fnp) mayRequeue = false;
-        }
-        if (mayRequeue) {
-            float bd = (mental_ball(w, mi, 500).flat() - h.spatial.position).length();
-            const bool pending = ca.frameNumber < ca.touchFrame;
-            if (((ca.functionType == kFtMovement && !pl.hasPossession && bd < 16.0f) ||
-                 (ca.functionType == kFtMovement && pl.hasPossession) ||
-                 (ca.functionType == kFtTrap && pending) || (ca.functionType == kFtBallControl && pending)) &&
-                (a.incomingSpecialState == kSS_Empty) && (a.outgoingSpecialState == kSS_Empty))
-                mayRequeue = true;
-            else
-                mayRequeue = false;
-        }
-        if (mayRequeue) h.interruptAnim = kIntReQueue;
-    }
-    if (h.interruptAnim != kIntNone) {
-        CommandQueue q;
-        if (h.interruptAnim == kIntTrip && h.tripType != 0) {
-            add_trip_commands(s, h, q, h.tripType);
-            h.tripType = 0;
-            PlayerCommand bmc;
-            basic_movement_command(bmc, h, h.spatial.floatVelocity);
-            queue_push(s, q, bmc);
-        } else {
-            q.count = 0;
-            if (!player_request_command(s, p, q)) return false;
-        }
-        bool found = false, preferPass = false;
-        for (int i = 0; i < q.count; i++) {
-            const PlayerCommand &c = q[i];
-            if (c.desiredFunctionType == kFtShortPass || c.desiredFunctionType == kFtLongPass ||
-                c.desiredFunctionType == kFtHighPass || c.desiredFunctionType == kFtShot)
-                preferPass = true;
-            Selector sel(s, p);
-            int r = sel.select(c, h.interruptAnim, preferPass);
-            if (r == kSelUnsupported) return s.fail(kStatusUnsupported);
-            if (*s.status != kStatusOk) return false;
-            found = r == kSelTrue;
-            if (found) break;
-        }
-        if (h.interruptAnim == kIntSwitch && !found) return s.fail(kStatusUnsupported);
-        if (found) {
-            h.startPosition = h.spatial.position;
-            h.startAngle = h.spatial.angle;
-            {
-                Selector sel(s, p);
-                Vec3 nsp;
-                float nsa;
-                sel.predicted_situation(nsp, nsa);
-                h.nextStartPosition = nsp;
-                set_radian(h.nextStartAngle, nsa);
-            }
-            h.applyBuffer.anim = ca.anim;
-            h.applyBuffer.smooth = true;
-            h.applyBuffer.smoothFactor = (h.interruptAnim == kIntSwitch && h.prevAnimFunctionType == kFtMovement &&
-                                          ca.functionType == kFtMovement)
-                                             ? 0.0f
-                                             : 1.0f;
-            if (ca.functionType == kFtShot) h.applyBuffer.smoothFactor = 0.8f;
-            if (ca.functionType == kFtShortPass || ca.functionType == kFtHighPass) h.applyBuffer.smoothFactor = 0.8f;
-            if (ca.functionType == kFtDeflect || ca.functionType == kFtSliding) h.applyBuffer.smoothFactor = 0.8f;
-            if (ca.functionType == kFtBallControl || ca.functionType == kFtTrap) h.applyBuffer.smoothFactor = 0.8f;
-            float ad = s.D(ca.anim).animDifficultyFactor;
-            if (ad > h.decayingDifficultyFactor) h.decayingDifficultyFactor = ad;
-            if (h.interruptAnim == kIntReQueue && h.prevAnimFunctionType == ca.functionType) h.requeueDelayFrames = 22;
-        }
-    }
-    h.requeueDelayFrames = h.requeueDelayFrames - 1 > 0 ? h.requeueDelayFrames - 1 : 0;
-    h.interruptAnim = kIntNone;
     const Anim &a = s.A(ca.anim);
-    {
-        float bdNow = (ball_predict(ball, 0).flat() - h.spatial.position).length();
-        float bdFut = (ball_predict(ball, 200).flat() - (h.spatial.position + h.spatial.movement * 0.2f)).length();
-        float ltb = last_touch_bias(w, p, 1500);
-        float oltb = team_last_touch_bias(w, 1 - teamID, 240);
-        if (p == w.m.designatedPossessionPlayer &&
-            ((ltb <= 0.01f && oltb <= 0.01f && ca.functionType == kFtMovement && bdNow < 0.6f && bdFut > 0.65f &&
-              bdFut > bdNow) ||
-             (ltb <= 0.7f && pl.hasPossession && ca.functionType == kFtTrip && bdNow < 0.4f)) &&
-            ball_predict(ball, 0).c[2] < 1.6f)
-            pl.triggerControlledBallCollision = true;
-    }
-    bool ctrlColl = pl.triggerControlledBallCollision;
-    if (ctrlColl) pl.triggerControlledBallCollision = false;
     const AnimDerived &d = s.D(ca.anim);
     auto nextBodyAngle = [&]() {
         return h.startAngle.value() + a.outgoingAngle.value() + a.outgoingBodyAngle.value() + ca.rotationSmuggle.end.value();
@@ -549,6 +503,82 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
             w.m.ballRetainer = -1;
         }
     }
+    return true;
+}
+
+// One tick of a player's humanoid.
+CB_HDNI bool humanoid_process(const Sim &s, int p) {
+    Match &w = s.w;
+    Player &pl = w.m.players[p];
+    Humanoid &h = pl.base.humanoid;
+    AnimationState &ca = h.anim;
+    const int teamID = w.playerTeamID[p];
+    const Team &team = team_by_id(w, teamID);
+    const Ball &ball = w.m.ball;
+    const int mi = mental_index(w, h.mentalImageTime);
+    h.decayingPositionOffset *= 0.95f;
+    if ((double)h.decayingPositionOffset.length() < 0.005) h.decayingPositionOffset = Vec3(0);
+    h.decayingDifficultyFactor = clampf_(h.decayingDifficultyFactor - 0.002f, 0.0f, 1.0f);
+    bool teamTouchedLast = w.m.lastTouchTeamID == teamID;
+    h.mentalImageTime = teamTouchedLast ? 0 : reaction_time_ms(s, p);
+    calc_spatial_state(s, h);
+    h.spatial.positionOffsetMovement = Vec3(0);
+    ca.frameNumber++;
+    h.prevAnimFrameNumber++;
+    {
+        const Anim &a = s.A(ca.anim);
+        if (ca.frameNumber == a.frameCount - 1 && h.interruptAnim == kIntNone) h.interruptAnim = kIntSwitch;
+        bool mayRequeue = true;
+        if (mayRequeue && h.interruptAnim != kIntNone) mayRequeue = false;
+        if (mayRequeue) {
+            bool fnp = false;
+            float ad = ((h.spatial.position + h.spatial.movement * 0.1f) - ball_predict(ball, 100).flat()).length();
+            uint64_t second = team_slot(w, teamID) == 1 ? 1 : 0;
+            uint64_t t = w.m.actualTime_ms;
+            if (w.m.designatedPossessionPlayer == p && ad < 3.0f) fnp = ((t + second * 10) % 20) == 0;
+            else if (w.m.designatedPossessionPlayer == p) fnp = ((t + second * 10) % 30) == 0;
+            else if (team.designatedTeamPossessionPlayer == p) fnp = ((t + second * 20) % 40) == 0;
+            else if (ad < 5.0f) fnp = ((t + second * 20) % 50) == 0;
+            else if (ad < 10.0f) fnp = ((t + second * 40) % 80) == 0;
+            if (!fnp) mayRequeue = false;
+        }
+        if (mayRequeue) {
+            float bd = (mental_ball(w, mi, 500).flat() - h.spatial.position).length();
+            const bool pending = ca.frameNumber < ca.touchFrame;
+            if (((ca.functionType == kFtMovement && !pl.hasPossession && bd < 16.0f) ||
+                 (ca.functionType == kFtMovement && pl.hasPossession) ||
+                 (ca.functionType == kFtTrap && pending) || (ca.functionType == kFtBallControl && pending)) &&
+                (a.incomingSpecialState == kSS_Empty) && (a.outgoingSpecialState == kSS_Empty))
+                mayRequeue = true;
+            else
+                mayRequeue = false;
+        }
+        if (mayRequeue) h.interruptAnim = kIntReQueue;
+    }
+    if (!warp_assisted(s, p, h.interruptAnim != kIntNone,
+                       [](const Sim &sim, int player) { return humanoid_interrupt(sim, player); }))
+        return false;
+    h.requeueDelayFrames = h.requeueDelayFrames - 1 > 0 ? h.requeueDelayFrames - 1 : 0;
+    h.interruptAnim = kIntNone;
+    const Anim &a = s.A(ca.anim);
+    {
+        float bdNow = (ball_predict(ball, 0).flat() - h.spatial.position).length();
+        float bdFut = (ball_predict(ball, 200).flat() - (h.spatial.position + h.spatial.movement * 0.2f)).length();
+        float ltb = last_touch_bias(w, p, 1500);
+        float oltb = team_last_touch_bias(w, 1 - teamID, 240);
+        if (p == w.m.designatedPossessionPlayer &&
+            ((ltb <= 0.01f && oltb <= 0.01f && ca.functionType == kFtMovement && bdNow < 0.6f && bdFut > 0.65f &&
+              bdFut > bdNow) ||
+             (ltb <= 0.7f && pl.hasPossession && ca.functionType == kFtTrip && bdNow < 0.4f)) &&
+            ball_predict(ball, 0).c[2] < 1.6f)
+            pl.triggerControlledBallCollision = true;
+    }
+    bool ctrlColl = pl.triggerControlledBallCollision;
+    if (ctrlColl) pl.triggerControlledBallCollision = false;
+    const bool touches = (ctrlColl && ca.touchFrame == -1) || ca.touchFrame == ca.frameNumber || w.m.ballRetainer == p;
+    if (!warp_assisted(s, p | (ctrlColl ? 0x10000 : 0), touches,
+                       [](const Sim &sim, int touchArg) { return humanoid_touches(sim, touchArg); }))
+        return false;
     const int eff = a.frameCount - 1;
     if (ca.touchFrame != -1 && ca.frameNumber <= ca.touchFrame) {
         float v = lm::lm_cosf((ca.frameNumber / (float)(ca.touchFrame + 1) - 0.5f) * kPi * 2.0f) + 1.0f;

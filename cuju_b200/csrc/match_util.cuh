@@ -88,6 +88,48 @@ struct Sim {
     }
 };
 
+// Runs fn(sim, arg) for the environment of every lane whose `need` is set and returns that lane's
+// result (true where not needed). In lane mode, when all 32 lanes of the warp execute this call
+// together, the calls are taken one environment at a time by the whole warp in warp mode, so the
+// wide loops inside them (animation filters, candidate sorts) split across 32 lanes instead of
+// running on one lane while the others wait; otherwise every lane makes its own call. `fn` must
+// read and write only device memory reachable from the Sim, never the calling lane's locals.
+#if CB_DEVICE_PASS
+__device__ __forceinline__ unsigned long long shfl_word(unsigned long long v, int src) {
+    return __shfl_sync(0xffffffffu, v, src);
+}
+#endif
+template <class Fn>
+CB_HD bool warp_assisted(const Sim &s, int arg, bool need, Fn fn) {
+#if CB_DEVICE_PASS
+    if (lane_env() && __activemask() == 0xffffffffu) {
+        unsigned pending = __ballot_sync(0xffffffffu, need);
+        bool mine = true;
+        while (pending) {
+            const int src = __ffs(pending) - 1;
+            pending &= pending - 1;
+            Match *w = reinterpret_cast<Match *>(shfl_word(reinterpret_cast<unsigned long long>(&s.w), src));
+            const Context *c =
+                reinterpret_cast<const Context *>(shfl_word(reinterpret_cast<unsigned long long>(&s.ctx), src));
+            WarpScratch *sc = reinterpret_cast<WarpScratch *>(shfl_word(reinterpret_cast<unsigned long long>(s.scratch), src));
+            int32_t *st = reinterpret_cast<int32_t *>(shfl_word(reinterpret_cast<unsigned long long>(s.status), src));
+            const int a = __shfl_sync(0xffffffffu, arg, src);
+            const Sim shared{*w, *c, sc, st};
+            __syncwarp();
+            if (lane_id() == 0) region_flag() = 0;
+            __syncwarp();
+            const bool r = fn(shared, a);
+            __syncwarp();
+            if (lane_id() == 0) region_flag() = 2;
+            __syncwarp();
+            if (lane_id() == src) mine = r;
+        }
+        return mine;
+    }
+#endif
+    return need ? fn(s, arg) : true;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Teams and humanoids. A team ID is 0/1 (scenario left/right); its slot is its place in
 // processing order; teams[0] is the team processed first.

@@ -250,9 +250,54 @@ CB_HDNI void referee_request_command(const Sim &s, int official, CommandQueue &q
     }
 }
 
+// The interrupt branch of an official's tick: the referee's command and the animation selection.
+// Reads and writes only the match, so a whole warp can run it for one environment.
+CB_HDNI bool official_interrupt(const Sim &s, int official) {
+    const int hi = s.w.m.playerCount + official;
+    Humanoid &h = s.w.m.officials[official].humanoid;
+    AnimationState &ca = h.anim;
+    CommandQueue q;
+    if (h.interruptAnim == kIntTrip && h.tripType != 0) {
+        add_trip_commands(s, h, q, h.tripType);
+        h.tripType = 0;
+        PlayerCommand bmc;
+        basic_movement_command(bmc, h, h.spatial.floatVelocity);
+        queue_push(s, q, bmc);
+    } else {
+        referee_request_command(s, official, q);
+    }
+    bool found = false;
+    for (int i = 0; i < q.count; i++) {
+        Selector sel(s, hi);
+        int r = sel.base_select(q[i], h.interruptAnim);
+        if (r == kSelUnsupported) return s.fail(kStatusUnsupported);
+        if (*s.status != kStatusOk) return false;
+        found = r == kSelTrue;
+        if (found) break;
+    }
+    if (found) {
+        h.startPosition = h.spatial.position;
+        h.startAngle = h.spatial.angle;
+        {
+            Selector sel(s, hi);
+            Vec3 nsp;
+            float nsa;
+            sel.predicted_situation(nsp, nsa);
+            h.nextStartPosition = nsp;
+            set_radian(h.nextStartAngle, nsa);
+        }
+        h.applyBuffer.anim = ca.anim;
+        h.applyBuffer.smooth = true;
+        h.applyBuffer.smoothFactor = (h.interruptAnim == kIntSwitch) ? 0.6f : 1.0f;
+        float ad = s.D(ca.anim).animDifficultyFactor;
+        if (ad > h.decayingDifficultyFactor) h.decayingDifficultyFactor = ad;
+        if (h.interruptAnim == kIntReQueue && h.prevAnimFunctionType == ca.functionType) h.requeueDelayFrames = 32;
+    }
+    return true;
+}
+
 CB_HDNI bool official_process(const Sim &s, int official) {
     Match &w = s.w;
-    const int hi = w.m.playerCount + official;
     Humanoid &h = w.m.officials[official].humanoid;
     AnimationState &ca = h.anim;
     h.decayingPositionOffset *= 0.95f;
@@ -263,45 +308,9 @@ CB_HDNI bool official_process(const Sim &s, int official) {
     ca.frameNumber++;
     h.prevAnimFrameNumber++;
     if (ca.frameNumber == s.A(ca.anim).frameCount - 1 && h.interruptAnim == kIntNone) h.interruptAnim = kIntSwitch;
-    if (h.interruptAnim != kIntNone) {
-        CommandQueue q;
-        if (h.interruptAnim == kIntTrip && h.tripType != 0) {
-            add_trip_commands(s, h, q, h.tripType);
-            h.tripType = 0;
-            PlayerCommand bmc;
-            basic_movement_command(bmc, h, h.spatial.floatVelocity);
-            queue_push(s, q, bmc);
-        } else {
-            referee_request_command(s, official, q);
-        }
-        bool found = false;
-        for (int i = 0; i < q.count; i++) {
-            Selector sel(s, hi);
-            int r = sel.base_select(q[i], h.interruptAnim);
-            if (r == kSelUnsupported) return s.fail(kStatusUnsupported);
-            if (*s.status != kStatusOk) return false;
-            found = r == kSelTrue;
-            if (found) break;
-        }
-        if (found) {
-            h.startPosition = h.spatial.position;
-            h.startAngle = h.spatial.angle;
-            {
-                Selector sel(s, hi);
-                Vec3 nsp;
-                float nsa;
-                sel.predicted_situation(nsp, nsa);
-                h.nextStartPosition = nsp;
-                set_radian(h.nextStartAngle, nsa);
-            }
-            h.applyBuffer.anim = ca.anim;
-            h.applyBuffer.smooth = true;
-            h.applyBuffer.smoothFactor = (h.interruptAnim == kIntSwitch) ? 0.6f : 1.0f;
-            float ad = s.D(ca.anim).animDifficultyFactor;
-            if (ad > h.decayingDifficultyFactor) h.decayingDifficultyFactor = ad;
-            if (h.interruptAnim == kIntReQueue && h.prevAnimFunctionType == ca.functionType) h.requeueDelayFrames = 32;
-        }
-    }
+    if (!warp_assisted(s, official, h.interruptAnim != kIntNone,
+                       [](const Sim &sim, int o) { return official_interrupt(sim, o); }))
+        return false;
     h.requeueDelayFrames = (int)clampf_((float)(h.requeueDelayFrames - 1), 0, 10000);
     h.interruptAnim = kIntNone;
     const Anim &pa = s.A(ca.anim);
