@@ -34,9 +34,9 @@ DIFFICULTY = (0.2, 0.2)
 ENVS_PER_GPU = 16384
 METRIC = 'env steps/sec, 11v11 at 1/2/4/8 B200 vs host-CPU path; % HBM roofline'
 STATE_BYTES = 106914  # serialized GRF state of 11_vs_11 with one left agent (measured by get_state)
-# DRAM bytes (read + write) per env-step of step_kernel: 14.173 GB over one 4,096-environment launch
+# DRAM bytes (read + write) per env-step of step_kernel: 13.660 GB over one 4,096-environment launch
 # (ncu --set full, dram__bytes_read.sum + dram__bytes_write.sum).
-TRAFFIC_PER_ENV_STEP = 14.173e9 / 4096
+TRAFFIC_PER_ENV_STEP = 13.660e9 / 4096
 
 
 def bytes_per_env_step(agents: int = 1, stack: int = 1, state: int = STATE_BYTES) -> int:
@@ -211,12 +211,22 @@ def run_b200(args) -> None:
     kernel_ms = [a.elapsed_time(b) for a, b in events]
     clock = clocks.summary()
 
-    # End to end through the public API: pinned host actions in, observation/reward/done out.
+    # End to end through the public API: pinned host actions in, observation/reward/done out. A
+    # fresh batch of the same configuration replays the same seeds, warm-up and actions, so the
+    # timed steps are the same simulated steps as above (a step's cost depends on the match
+    # situation, and a second episode of the same batch would play the mirrored variant).
     host_actions = actions[args.warmup:].cpu().pin_memory()
     obs_host = torch.empty((envs, agents, 115), dtype=torch.float32, pin_memory=True)
     reward_host = torch.empty((envs, agents), dtype=torch.float32, pin_memory=True)
     done_host = torch.empty((envs,), dtype=torch.bool, pin_memory=True)
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    e2e_steps = max(1, min(args.steps, args.e2e_steps if args.e2e_steps else args.steps))
+    batch.close()
+    batch = BatchEnvironment(ASSETS, environment_count=envs, seed=0, device=device, difficulty=[DIFFICULTY],
+                             first_index=rank * envs)
+    batch.reset(seeds=torch.arange(rank * envs, (rank + 1) * envs))
+    for step in range(args.warmup):
+        batch.step(actions[step], synchronize=False)
+    batch.synchronize()
     barrier()
     e_begin = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
@@ -282,8 +292,8 @@ def main() -> None:
     parser.add_argument('--warmup', type=int, default=3)
     parser.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     parser.add_argument('--envs', type=int, default=ENVS_PER_GPU)
-    parser.add_argument('--e2e-steps', type=int, default=10)
-    parser.add_argument('--cpu-steps', type=int, default=10)
+    parser.add_argument('--e2e-steps', type=int, default=0, help='end-to-end steps (default: --steps)')
+    parser.add_argument('--cpu-steps', type=int, default=60)
     parser.add_argument('--no-cpu-baseline', dest='cpu_baseline', action='store_false')
     args = parser.parse_args()
     if args.impl == 'reference':
