@@ -1,0 +1,86 @@
+"""GPU parity at sizes where the lanes of every warp are all busy.
+
+The kernels run one environment per lane and, when all 32 lanes of a warp reach a humanoid's
+command request, animation selection or ball touch together, run that branch with the whole warp
+for one environment at a time. Batches smaller than a warp never take that path, so these tests
+use full warps: a 64-environment 11v11 batch compared step by step with the reference CPU backend,
+and the bench workload itself (16,384 environments) with a sample of its environments compared
+against single-environment reference batches. The seed rule makes environment i identical in
+any batch that holds it (`first_index` = i for a batch of one), so the sample checks the full-size
+run without stepping 16,384 environments on the CPU.
+"""
+
+import pytest
+import torch
+
+from conftest import ANIMATIONS, needs_data, resolve
+
+pytestmark = [pytest.mark.gpu, needs_data]
+
+ASSETS = '11_vs_11_stochastic_l1_r0'
+DIFFICULTY = (0.2, 0.2)
+
+
+def _row_bytes(tensor, index):
+    return tensor[index].detach().cpu().contiguous().numpy().tobytes()
+
+
+def test_11v11_full_warps_against_the_oracle():
+    from cuju_b200 import BatchEnvironment
+    from oracle.driver import OracleBatch
+
+    envs, steps = 64, 40
+    paths, counts = resolve(ASSETS)
+    mine = BatchEnvironment(ASSETS, environment_count=envs, seed=11, difficulty=[DIFFICULTY])
+    ref = OracleBatch(paths, counts, envs, 11, ANIMATIONS, threads=0, difficulty=list(DIFFICULTY) * envs)
+    try:
+        generator = torch.Generator().manual_seed(3)
+        mine.reset()
+        expected = ref.reset()
+        obs, reward, done, _, score = mine._outputs()
+        assert obs.cpu().numpy().tobytes() == expected[0], 'reset observations differ'
+        for step in range(steps):
+            actions = torch.randint(0, 19, (envs, mine.agents), generator=generator, dtype=torch.int32)
+            mine.step(actions.cuda())
+            expected = ref.step(actions.flatten().tolist())
+            got = tuple(t.cpu().numpy().tobytes() for t in (mine._outputs()[i] for i in (0, 1, 2, 4)))
+            for name, a, b in zip(('simple115', 'reward', 'done', 'score_reward'), got, expected):
+                assert a == b, f'{name} differs at step {step}'
+        for index in range(envs):
+            assert mine.engine_state(index)[0] == ref.engine_state(index)[0], f'state {index} differs'
+    finally:
+        mine.close()
+        ref.close()
+
+
+def test_bench_workload_sampled_environments_match_the_oracle():
+    from cuju_b200 import BatchEnvironment
+    from oracle.driver import OracleBatch
+
+    envs, steps = 16384, 12
+    sample = [0, 1, 31, 32, 4097, 8191, 12345, 16383]
+    paths, counts = resolve(ASSETS)
+    mine = BatchEnvironment(ASSETS, environment_count=envs, seed=0, difficulty=[DIFFICULTY])
+    refs = {e: OracleBatch(paths, counts, 1, 0, ANIMATIONS, threads=1, difficulty=list(DIFFICULTY), first_index=e)
+            for e in sample}
+    try:
+        generator = torch.Generator().manual_seed(9)
+        mine.reset(seeds=torch.arange(envs))
+        for e, ref in refs.items():
+            expected = ref.reset([e])
+            assert _row_bytes(mine._outputs()[0], e) == expected[0], f'reset of environment {e} differs'
+        for step in range(steps):
+            actions = torch.randint(0, 19, (envs, mine.agents), generator=generator, dtype=torch.int32)
+            mine.step(actions.cuda())
+            obs, reward, done, _, score = mine._outputs()
+            for e, ref in refs.items():
+                expected = ref.step(actions[e].tolist())
+                got = (_row_bytes(obs, e), _row_bytes(reward, e), _row_bytes(done, e), _row_bytes(score, e))
+                for name, a, b in zip(('simple115', 'reward', 'done', 'score_reward'), got, expected):
+                    assert a == b, f'{name} of environment {e} differs at step {step}'
+        for e, ref in refs.items():
+            assert mine.engine_state(e)[0] == ref.engine_state(0)[0], f'state of environment {e} differs'
+    finally:
+        mine.close()
+        for ref in refs.values():
+            ref.close()
