@@ -133,6 +133,13 @@ def cpu_reference(args, envs: int, steps: int, warmup: int, threads: int) -> dic
     return {'value': envs * steps / elapsed, 'elapsed_s': elapsed, 'envs': envs, 'steps': steps}
 
 
+def workload_config(envs: int, world: int) -> dict:
+    return {'workload': f'{ASSETS}, 1 controlled agent, difficulty {DIFFICULTY}, {envs} envs per GPU, '
+                        'auto-reset, seeded uniform int32 actions in [0,19)',
+            'envs_per_gpu': envs, 'parallelism': f'env-slice x{world}',
+            'l2': 'state larger than L2 (16,384 x ~370 KB worlds), no flush needed'}
+
+
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -153,10 +160,10 @@ def run_reference(args) -> None:
         'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': 'env steps/s', 'n_gpus': args.gpus,
         'steps': steps, 'warmup': args.warmup, 'ms_per_step': 1000 * result['elapsed_s'] / steps,
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': f'{ASSETS} difficulty {DIFFICULTY}, {envs} envs (16 per host thread), seeded '
-                               'uniform actions, auto-reset'},
+        'config': workload_config(args.envs, args.gpus),
         'cpu_baseline': {'value': value, 'unit': 'env steps/s', 'cores': threads, 'kind': 'reference',
-                         'sample': f'{envs} envs x {steps} steps after {args.warmup} warm-up steps'},
+                         'sample': f'{envs} envs (16 per host thread) x {steps} steps after {args.warmup} '
+                                   'warm-up steps of the same workload, reference CPU backend built from source'},
         'e2e': {'value': value, 'unit': 'env steps/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
@@ -258,10 +265,7 @@ def run_b200(args) -> None:
             'metric': METRIC, 'value': value, 'unit': 'env steps/s', 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': elapsed_ms / args.steps, 'higher_is_better': True,
             'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-            'config': {'workload': f'{ASSETS}, 1 controlled agent, difficulty {DIFFICULTY}, {envs} envs per GPU, '
-                                   'auto-reset, seeded uniform int32 actions in [0,19)',
-                       'envs_per_gpu': envs, 'parallelism': f'env-slice x{world}',
-                       'l2': 'state larger than L2 (16,384 x ~370 KB worlds), no flush needed'},
+            'config': workload_config(envs, world),
             'e2e': {'value': e2e_value, 'unit': 'env steps/s', 'h2d_bytes_per_step': 4 * envs * agents,
                     'd2h_bytes_per_step': envs * agents * 115 * 4 + envs * agents * 4 + envs},
             'gpu_launches': args.steps,
