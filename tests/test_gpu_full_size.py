@@ -7,13 +7,16 @@ use full warps: a 64-environment 11v11 batch compared step by step with the refe
 and the bench workload itself (16,384 environments) with a sample of its environments compared
 against single-environment reference batches. The seed rule makes environment i identical in
 any batch that holds it (`first_index` = i for a batch of one), so the sample checks the full-size
-run without stepping 16,384 environments on the CPU.
+run without stepping 16,384 environments on the CPU. Where the reference's CUDA backend has been
+built from its sources (`make -C oracle cuda`), the whole bench batch is also compared with it.
 """
+
+import os
 
 import pytest
 import torch
 
-from conftest import ANIMATIONS, needs_data, resolve
+from conftest import ANIMATIONS, ROOT, needs_data, resolve
 
 pytestmark = [pytest.mark.gpu, needs_data]
 
@@ -84,3 +87,40 @@ def test_bench_workload_sampled_environments_match_the_oracle():
         mine.close()
         for ref in refs.values():
             ref.close()
+
+
+REFERENCE_CUDA = os.path.join(ROOT, 'oracle', '_ref', 'libcuju_cuda.so')
+
+
+@pytest.mark.skipif(not os.path.isfile(REFERENCE_CUDA), reason='run make -C oracle cuda to build the reference GPU backend')
+def test_bench_workload_equals_the_reference_cuda_backend():
+    """The whole 16,384-environment bench batch against the reference's own CUDA backend, compiled
+    from its sources for sm_100a (oracle/Makefile, target `cuda`) and driven through the same C-ABI:
+    every output buffer, every step."""
+    import hashlib
+
+    from cuju_b200 import BatchEnvironment
+
+    envs, steps = 16384, 6
+    digests = {}
+    for name, library in (('b200', None), ('reference', REFERENCE_CUDA)):
+        options = {'library': library} if library else {}
+        batch = BatchEnvironment(ASSETS, environment_count=envs, seed=0, difficulty=[DIFFICULTY], **options)
+        try:
+            generator = torch.Generator(device='cuda').manual_seed(21)
+            batch.reset(seeds=torch.arange(envs))
+            trail = [hashlib.sha256(_row_bytes(batch._outputs()[0], slice(None))).hexdigest()]
+            for step in range(steps):
+                actions = torch.randint(0, 19, (envs, batch.agents), generator=generator, device='cuda',
+                                        dtype=torch.int32)
+                batch.step(actions)
+                obs, reward, done, _, score = batch._outputs()
+                h = hashlib.sha256()
+                for t in (obs, reward, done, score):
+                    h.update(_row_bytes(t, slice(None)))
+                trail.append(h.hexdigest())
+            digests[name] = trail
+        finally:
+            batch.close()
+    for step, (a, b) in enumerate(zip(digests['b200'], digests['reference'])):
+        assert a == b, f'outputs differ from the reference CUDA backend at step {step}'
