@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -442,6 +443,79 @@ public:
         const Scenario &sc = variant(hostSlots[e].bundle * 4 + (cfg.episodeNumber & 1)).world->scenario;
         return side == 0 ? sc.leftTeamDifficulty : sc.rightTeamDifficulty;
     }
+    // batch_environment.h:396 (SetState). The state's scenario picks the variant (of the
+    // environment's bundle) to continue from; its difficulties must be the environment's. The
+    // observation is computed on the host from the loaded world, reward, done and score restart at
+    // zero, and the outputs are written as after a reset.
+    void set_state(int e, const std::string &bytes, int prevScoreDiff, int prevGameMode, int prevBallOwnedTeam,
+                   const int32_t *collected) {
+        check_env(e);
+        check(cudaDeviceSynchronize(), "set_state");
+        std::unique_ptr<Match> w(new Match);
+        Codec codec;
+        codec.animationCount = (int)store->anims.size();
+        if (!codec.load_frame(bytes, *w))
+            throw std::invalid_argument("expected the bytes of a state, found bytes that do not load");
+        const int bundle = hostSlots[e].bundle;
+        // The scenario compares without the state's real_time flag; the bundle's stands in.
+        const bool realTime = w->scenario.realTime;
+        w->scenario.realTime = bundles[bundle].variants[0].world->scenario.realTime;
+        const std::string sc = save_scenario(*w);
+        int parity = 0;
+        while (parity < 4 && bundles[bundle].variants[parity].scenario != sc) parity++;
+        if (parity == 4) throw std::invalid_argument("expected a state of the scenario of the environment, found another");
+        w->scenario.realTime = realTime;
+        const Scenario &own = bundles[bundle].variants[parity].world->scenario;
+        float expected[2] = {own.leftTeamDifficulty, own.rightTeamDifficulty};
+        for (int side = 0; side < 2; side++)
+            if (!hostDifficulty.empty() && hostDifficulty[e * 2 + side] >= 0.0f) expected[side] = hostDifficulty[e * 2 + side];
+        if (memcmp(&w->scenario.leftTeamDifficulty, &expected[0], 4) != 0 ||
+            memcmp(&w->scenario.rightTeamDifficulty, &expected[1], 4) != 0)
+            throw std::invalid_argument("expected a state of the difficulties of the environment, " +
+                                        std::to_string(expected[0]) + " and " + std::to_string(expected[1]) +
+                                        ", found " + std::to_string(w->scenario.leftTeamDifficulty) + " and " +
+                                        std::to_string(w->scenario.rightTeamDifficulty));
+        const int variantIndex = bundle * 4 + parity;
+        const AssetVariant &av = bundles[bundle].variants[parity];
+        std::unique_ptr<EnvCore> core(new EnvCore{});
+        core->previousScoreDifference = prevScoreDiff;
+        core->previousGameMode = prevGameMode;
+        core->previousBallOwnedTeam = prevBallOwnedTeam;
+        Context ctx{};
+        ctx.staticData = &av.staticData;
+        ctx.skeletons = av.skeletons.data();
+        ctx.ticksPerStep = cfg.ticksPerStep;
+        environment_get_state(*w, ctx, core->observation);
+        EnvSlot slot;
+        check(cudaMemcpy(&slot, b.slots + e, sizeof(EnvSlot), cudaMemcpyDeviceToHost), "set_state");
+        slot.variant = variantIndex;
+        const int agents = slot.leftAgents + slot.rightAgents;
+        for (int a = 0; a < kAgentsMax; a++) slot.collected[a] = collected && a < agents ? collected[a] : 0;
+        for (int a = 0; a < agents; a++) {
+            const bool left = a < slot.leftAgents;
+            for (int i = 0; i < sticky_count(b.actionSet); i++)
+                slot.sticky[a][i] = sticky_action_state(*w, sticky_action(i), left, left ? a : a - slot.leftAgents);
+        }
+        // A sent-off keeper's hand-over lives outside the state, so it carries over.
+        check(cudaMemcpy(w->formationOverride, b.worlds[e].formationOverride, sizeof(w->formationOverride),
+                         cudaMemcpyDeviceToHost),
+              "set_state");
+        check(cudaMemcpy(b.worlds + e, w.get(), sizeof(Match), cudaMemcpyHostToDevice), "set_state");
+        check(cudaMemcpy(b.cores + e, core.get(), sizeof(EnvCore), cudaMemcpyHostToDevice), "set_state");
+        check(cudaMemcpy(b.slots + e, &slot, sizeof(EnvSlot), cudaMemcpyHostToDevice), "set_state");
+        check(cudaMemset(b.reward + (size_t)e * b.agents, 0, sizeof(float) * b.agents), "set_state");
+        check(cudaMemset(b.done + e, 0, 1), "set_state");
+        check(cudaMemset(b.scoreReward + e, 0, sizeof(int32_t)), "set_state");
+        check(cudaMemset(b.status + e, 0, sizeof(int32_t)), "set_state");
+        check(cudaMemset(outputMaskDev, 0, (size_t)b.count), "set_state");
+        check(cudaMemset(outputMaskDev + e, 1, 1), "set_state");
+        check(launch_outputs(b, outputMaskDev, nullptr), "set_state outputs");
+        check(cudaDeviceSynchronize(), "set_state");
+        if (!started[e]) {
+            started[e] = true;
+            unstarted--;
+        }
+    }
     std::string get_state(int e, EnvCore &core, EnvSlot &slot) {
         check_env(e);
         check(cudaDeviceSynchronize(), "get_state");
@@ -657,9 +731,15 @@ const char *cuju_environment_get_state(void *env, int index, unsigned long long 
         return nullptr;
     }
 }
-int cuju_environment_set_state(void *, int, const char *, unsigned long long, const int *) {
-    lastError = "set_state is not available in this backend yet";
-    return -1;
+int cuju_environment_set_state(void *env, int index, const char *bytes, unsigned long long size, const int *episode) {
+    try {
+        if (!bytes || !episode) throw std::invalid_argument("expected state bytes and episode values");
+        static_cast<BatchEnv *>(env)->set_state(index, std::string(bytes, size), episode[0], episode[1], episode[2],
+                                                episode + 3);
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
 }
 int cuju_environment_set_stack(void *, int, const char *, const void *, unsigned long long) {
     lastError = "set_stack is not available in this backend yet";

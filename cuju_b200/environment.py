@@ -10,7 +10,9 @@ engine state; python/cuju/_batch/state.py:44-77).
 from __future__ import annotations
 
 import ctypes
+import io
 import os
+import pickle
 import re
 import struct
 from typing import Any
@@ -99,8 +101,27 @@ def pickle_episode(episode: list[int], collected: list[int] | None) -> bytes:
     return data + b'u.'
 
 
+class _Stub:
+    """Stands in for any class a GRF state pickle names; BUILD fills its __dict__."""
+
+
+class _EpisodeUnpickler(pickle.Unpickler):
+    def find_class(self, module, name):
+        return _Stub
+
+
+def unpickle_episode(data: bytes, agents: int) -> list[int]:
+    """The episode values (3 + agents) of GRF's state pickle: score difference, game mode and
+    ball-owning team after the previous step, then each agent's collected checkpoints."""
+    state = _EpisodeUnpickler(io.BytesIO(data)).load()
+    core = state['FootballEnvCore'].__dict__
+    values = [int(core['previous_score_diff']), int(core['previous_game_mode']), int(core['prev_ball_owned_team'])]
+    collected = state.get('CheckpointRewardWrapper', {})
+    return values + [int(collected.get(agent, 0)) for agent in range(agents)]
+
+
 class BatchEnvironment:
-    """A batch of GRF environments stepped on one B200, one warp per environment."""
+    """A batch of GRF environments stepped on one B200, one lane per environment."""
 
     def __init__(
         self,
@@ -289,6 +310,23 @@ class BatchEnvironment:
         collected = episode[3: 3 + self.agents] if self._checkpoints else None
         data = pickle_episode(episode[:3], collected)
         return struct.pack('<i', len(data)) + data + match
+
+    def set_engine_state(self, index: int, match: bytes, episode: list[int]) -> None:
+        """Sets environment `index` to GRF engine bytes and its episode values (3 + agents), as
+        `engine_state` returns them; the state's scenario and difficulties must be the
+        environment's. Reward, done and score restart at zero and the outputs are rewritten."""
+        values = (ctypes.c_int * (3 + _native.MAXIMUM_AGENTS))(*list(episode)[:3 + _native.MAXIMUM_AGENTS])
+        torch.cuda.synchronize(self._torch_device)
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_set_state(
+                self._handle, index, ctypes.c_char_p(match), len(match), values))
+
+    def set_state(self, index: int, state: bytes) -> None:
+        """Sets environment `index` from GRF's state bytes (episode pickle, then engine), as
+        `get_state` writes them."""
+        size = struct.unpack_from('<i', state)[0]
+        episode = unpickle_episode(state[4:4 + size], self.agents)
+        self.set_engine_state(index, state[4 + size:], episode)
 
     def episode(self, index: int) -> list[int]:
         values = (ctypes.c_longlong * 17)()

@@ -100,6 +100,13 @@ class OracleBatch:
             raise RuntimeError(self.lib.cuju_last_error().decode())
         return ctypes.string_at(p, size.value), list(episode)
 
+    def set_state(self, index, data, episode):
+        values = (ctypes.c_int * 25)(*list(episode)[:25])
+        self.lib.cuju_environment_set_state.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p,
+                                                        ctypes.c_ulonglong, ctypes.c_void_p]
+        self._check(self.lib.cuju_environment_set_state(self.handle, index, data, len(data), values))
+        return self.outputs()
+
     def close(self):
         if self.handle:
             self.lib.cuju_environment_destroy(self.handle)

@@ -103,3 +103,10 @@ def test_a_planted_difference_changes_the_oracle_digest():
     g = golden()
     entry = g['cases']['1_vs_1_easy/simple115v2']
     assert oracle_digest(entry['assets'], g['steps'], seed=g['seed'] + 1, environments=g['environments']) != entry['digest']
+
+
+def test_episode_pickle_reads_back():
+    from cuju_b200.environment import pickle_episode, unpickle_episode
+
+    assert unpickle_episode(pickle_episode([0, 0, -1], None), 2) == [0, 0, -1, 0, 0]
+    assert unpickle_episode(pickle_episode([2, 3, 1], [0, 4, 1, 0]), 4) == [2, 3, 1, 0, 4, 1, 0]
