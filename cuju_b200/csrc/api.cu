@@ -516,6 +516,22 @@ public:
             unstarted--;
         }
     }
+    // stacked_state.h:23 (SetStackedFrames), simple115 only: the observation stack of environment
+    // `e` after set_state, `[agents][115 * stack]` float32, the oldest frame first.
+    void set_stack(int e, const std::string &name, const void *frames, size_t size) {
+        check_env(e);
+        if (b.stack < 2) throw std::invalid_argument("expected a batch that stacks its observations");
+        if (name != "simple115") throw std::invalid_argument("expected the stack simple115 of the batch, found " + name);
+        const size_t agents = (size_t)(hostSlots[e].leftAgents + hostSlots[e].rightAgents);
+        const size_t width = (size_t)kSimple115 * b.stack;
+        const size_t expected = agents * width * sizeof(float);
+        if (size != expected)
+            throw std::invalid_argument("expected a stack of " + std::to_string(expected) +
+                                        " bytes for the agents of environment " + std::to_string(e) + ", found " +
+                                        std::to_string(size));
+        check(cudaDeviceSynchronize(), "set_stack");
+        check(cudaMemcpy(b.simple115 + (size_t)e * b.agents * width, frames, size, cudaMemcpyHostToDevice), "set_stack");
+    }
     std::string get_state(int e, EnvCore &core, EnvSlot &slot) {
         check_env(e);
         check(cudaDeviceSynchronize(), "get_state");
@@ -741,9 +757,14 @@ int cuju_environment_set_state(void *env, int index, const char *bytes, unsigned
         return fail(e);
     }
 }
-int cuju_environment_set_stack(void *, int, const char *, const void *, unsigned long long) {
-    lastError = "set_stack is not available in this backend yet";
-    return -1;
+int cuju_environment_set_stack(void *env, int index, const char *name, const void *frames, unsigned long long size) {
+    try {
+        if (!name || !frames) throw std::invalid_argument("expected a stack name and its frames");
+        static_cast<BatchEnv *>(env)->set_stack(index, name, frames, size);
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
 }
 void *cuju_environment_buffer(void *env, const char *name) {
     const cb::Batch &b = static_cast<BatchEnv *>(env)->b;

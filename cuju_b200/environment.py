@@ -328,6 +328,15 @@ class BatchEnvironment:
         episode = unpickle_episode(state[4:4 + size], self.agents)
         self.set_engine_state(index, state[4 + size:], episode)
 
+    def set_stack(self, index: int, frames: bytes) -> None:
+        """Writes the simple115 observation stack of environment `index` after `set_state`:
+        float32 `[agents][115 * stack]`, the oldest frame first (a stacked batch only)."""
+        data = bytes(frames)
+        torch.cuda.synchronize(self._torch_device)
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_set_stack(
+                self._handle, index, b'simple115', ctypes.c_char_p(data), len(data)))
+
     def episode(self, index: int) -> list[int]:
         values = (ctypes.c_longlong * 17)()
         self._check(self._library.cuju_environment_episode(self._handle, index, values, None))

@@ -3,6 +3,7 @@ CPU backend and loaded into both batches gives the same outputs at once and over
 steps, and the loaded bytes read back unchanged. The full GRF byte format (episode pickle, then
 engine bytes) round-trips through the Python mirror."""
 
+import ctypes
 import random
 
 import pytest
@@ -75,3 +76,39 @@ def test_set_state_refuses_another_scenario():
     finally:
         mine.close()
         other.close()
+
+
+def test_set_stack_restores_a_stacked_observation():
+    from cuju_b200 import BatchEnvironment
+    from oracle.driver import OracleBatch
+
+    envs, assets = 4, '5_vs_5_l4_r0'
+    paths, counts = resolve(assets)
+    mine = BatchEnvironment(assets, environment_count=envs, seed=2, stacked=True)
+    ref = OracleBatch(paths, counts, envs, 2, ANIMATIONS, threads=0, stack=4)
+    rng = random.Random(6)
+    try:
+        mine.reset()
+        assert _outputs(mine) == ref.reset()
+
+        def step_both(steps):
+            for step in range(steps):
+                acts = [[rng.randrange(19) for _ in range(mine.agents)] for _ in range(envs)]
+                mine.step(torch.tensor(acts, dtype=torch.int32).cuda())
+                assert _outputs(mine) == ref.step([x for row in acts for x in row]), f'step {step} differs'
+
+        step_both(12)
+        data, episode = ref.engine_state(2)
+        width = mine.agents * 115 * 4 * 4
+        frames = ref.outputs()[0][2 * width:3 * width]
+        ref.set_state(0, data, episode)
+        ref.lib.cuju_environment_set_stack.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p,
+                                                       ctypes.c_char_p, ctypes.c_ulonglong]
+        assert ref.lib.cuju_environment_set_stack(ref.handle, 0, b'simple115', frames, len(frames)) == 0
+        mine.set_engine_state(0, data, episode)
+        mine.set_stack(0, frames)
+        assert _outputs(mine) == ref.outputs(), 'outputs after set_state and set_stack differ'
+        step_both(12)
+    finally:
+        mine.close()
+        ref.close()
