@@ -127,10 +127,14 @@ public:
         mem.context = c.allocatorContext;
         if ((c.observation & kObsSimple115) && (c.observation & kObsSimple115v2))
             throw std::invalid_argument("simple115 and simple115v2 are exclusive");
-        if (c.observation & (kObsSmm | kObsRaw))
-            throw std::invalid_argument("this backend writes the simple115 representations only");
-        if (!(c.observation & (kObsSimple115 | kObsSimple115v2)))
-            throw std::invalid_argument("expected the simple115 or simple115v2 representation");
+        if (c.observation & kObsRaw)
+            throw std::invalid_argument("this backend writes the simple115 and extracted (SMM) representations only");
+        if (!(c.observation & (kObsSimple115 | kObsSimple115v2 | kObsSmm)))
+            throw std::invalid_argument("expected the simple115, simple115v2 or extracted representation");
+        if ((c.observation & kObsSmm) &&
+            (c.smmWidth < 1 || c.smmHeight < 1 || c.smmWidth > 4096 || c.smmHeight > 4096))
+            throw std::invalid_argument("expected SMM dimensions from 1 to 4096, found " + std::to_string(c.smmWidth) +
+                                        " x " + std::to_string(c.smmHeight));
         if (c.assets.empty()) throw std::invalid_argument("expected an asset bundle");
         if (c.ticksPerStep < 1)
             throw std::invalid_argument("expected at least one tick in a step, found " + std::to_string(c.ticksPerStep));
@@ -234,8 +238,21 @@ public:
         b.reward = alloc<float>((size_t)c.count * agents);
         b.done = alloc<uint8_t>(c.count);
         b.scoreReward = alloc<int32_t>(c.count);
-        b.simple115 = alloc<float>((size_t)c.count * agents * kSimple115 * c.stack);
-        b.finalSimple115 = alloc<float>((size_t)c.count * agents * kSimple115 * c.stack);
+        if (c.observation & (kObsSimple115 | kObsSimple115v2)) {
+            b.simple115 = alloc<float>((size_t)c.count * agents * kSimple115 * c.stack);
+            b.finalSimple115 = alloc<float>((size_t)c.count * agents * kSimple115 * c.stack);
+        }
+        b.smmWidth = c.smmWidth;
+        b.smmHeight = c.smmHeight;
+        if (c.observation & kObsSmm) {
+            // Zero maps and no marks: the first write paints onto a clear map.
+            const size_t map = (size_t)c.smmWidth * c.smmHeight * kSmmLayers * c.stack;
+            const size_t marks = (size_t)kSmmMarkRow * c.stack;
+            b.smm = alloc<uint8_t>((size_t)c.count * agents * map);
+            b.finalSmm = alloc<uint8_t>((size_t)c.count * agents * map);
+            b.smmMarks = alloc<int32_t>((size_t)c.count * agents * marks);
+            b.finalSmmMarks = alloc<int32_t>((size_t)c.count * agents * marks);
+        }
         b.teamDifficulty = nullptr;
         actionsDev = alloc<int32_t>((size_t)c.count * agents);
         maskDev = alloc<uint8_t>(c.count);
@@ -521,7 +538,8 @@ public:
     void set_stack(int e, const std::string &name, const void *frames, size_t size) {
         check_env(e);
         if (b.stack < 2) throw std::invalid_argument("expected a batch that stacks its observations");
-        if (name != "simple115") throw std::invalid_argument("expected the stack simple115 of the batch, found " + name);
+        if (name != "simple115" || !b.simple115)
+            throw std::invalid_argument("expected the stack simple115 of the batch, found " + name);
         const size_t agents = (size_t)(hostSlots[e].leftAgents + hostSlots[e].rightAgents);
         const size_t width = (size_t)kSimple115 * b.stack;
         const size_t expected = agents * width * sizeof(float);
@@ -771,6 +789,8 @@ void *cuju_environment_buffer(void *env, const char *name) {
     const std::string n = name;
     if (n == "simple115") return b.simple115;
     if (n == "final_simple115") return b.finalSimple115;
+    if (n == "smm") return b.smm;
+    if (n == "final_smm") return b.finalSmm;
     if (n == "reward") return b.reward;
     if (n == "done") return b.done;
     if (n == "score_reward") return b.scoreReward;

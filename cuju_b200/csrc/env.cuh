@@ -545,6 +545,11 @@ CB_HDNI float checkpoint_reward(const AgentView &v, float reward, int &collected
 
 enum { kObsSimple115 = 1, kObsSimple115v2 = 2, kObsSmm = 4, kObsRaw = 8 };
 constexpr int kSimple115 = 115;
+// GRF's super mini map ("extracted"): kSmmLayers channels per cell (left team, right team, ball,
+// active player), 255 at marked cells and 0 elsewhere.
+constexpr int kSmmLayers = 4;
+constexpr int kSmmMarks = 2 * kTeamPlayers + 2;  // every player, the ball, the active player
+constexpr int kSmmMarkRow = 1 + kSmmMarks;       // a frame's mark count, then its marks
 
 // Per-environment books (batch_core.h:343 EnvironmentSlot).
 struct EnvSlot {
@@ -581,7 +586,10 @@ struct Batch {
     int actionSet, observation;
     bool checkpoints, numpyLegacy, autoReset;
     int stack;
-    float *simple115, *finalSimple115;  // [count][agents][115 * stack]
+    float *simple115, *finalSimple115;  // [count][agents][115 * stack], null without simple115
+    uint8_t *smm, *finalSmm;            // [count][agents][smmHeight][smmWidth][4 * stack], or null
+    int32_t *smmMarks, *finalSmmMarks;  // [count][agents][stack][kSmmMarkRow]: each frame's marks
+    int smmWidth, smmHeight;
     float *reward;                      // [count][agents]
     uint8_t *done;                      // [count]
     int32_t *scoreReward;               // [count]
@@ -650,6 +658,68 @@ CB_HDNI bool reset_environment(const Batch &b, int e, const int64_t *seeds, cons
     return true;
 }
 
+/// observation_encoding.h:124 (SmmIndex): the byte of `layer` at the cell of a position in the
+/// observation's coordinates (x in [-1, 1], y in [-1/2.25, 1/2.25]), truncated toward zero in
+/// double and clamped into the map.
+CB_HD int smm_cell(int layer, double x, double y, int width, int height) {
+    const double x0 = -1.0, x1 = 1.0, y0 = -1.0 / 2.25, y1 = 1.0 / 2.25;
+    int col = cvt_d_i32((x - x0) / (x1 - x0) * width);
+    int row = cvt_d_i32((y - y0) / (y1 - y0) * height);
+    col = col < 0 ? 0 : (col > width - 1 ? width - 1 : col);
+    row = row < 0 ? 0 : (row > height - 1 ? height - 1 : row);
+    return (row * width + col) * kSmmLayers + layer;
+}
+/// observation_encoding.h:135 (SmmMarks): the marked bytes of one frame, in GRF's drawing order.
+CB_HD int smm_frame_marks(const AgentView &v, int32_t *marks, int width, int height) {
+    int n = 0;
+    for (int t = 0; t < 2; t++)
+        for (int p = 0; p < v.o.team[t].count; p++)
+            marks[n++] = smm_cell(t, v.o.team[t].players[p].position[0], v.o.team[t].players[p].position[1], width,
+                                  height);
+    marks[n++] = smm_cell(2, v.o.ball[0], v.o.ball[1], width, height);
+    if (v.active != -1)
+        marks[n++] = smm_cell(3, v.o.team[0].players[v.active].position[0],
+                              v.o.team[0].players[v.active].position[1], width, height);
+    return n;
+}
+// Sets (or clears) every marked byte of a stacked map: frame f of the stack sits at channels
+// [4 f, 4 f + 4) of each cell, and a mark names a byte of one frame.
+CB_HD void smm_paint(uint8_t *map, const int32_t *marks, int stack, uint8_t value) {
+    const int channels = kSmmLayers * stack;
+    for (int f = 0; f < stack; f++) {
+        const int32_t *row = marks + f * kSmmMarkRow;
+        for (int k = 0; k < row[0]; k++) {
+            const int m = row[1 + k];
+            map[(size_t)(m / kSmmLayers) * channels + kSmmLayers * f + m % kSmmLayers] = value;
+        }
+    }
+}
+/// batch_core.h:534 (the SMM part of WriteAgentOutputs). A map is zero but for its marks, so a
+/// write clears the previous marks, moves the frames one place toward the oldest (a reset fills
+/// every frame with the new one), and paints the marks again; the final map of an ended episode
+/// copies the same way.
+CB_HDNI void write_agent_smm(const Batch &b, size_t out, const AgentView &v, bool afterStep, bool finished) {
+    const int stack = b.stack;
+    const size_t mapBytes = (size_t)b.smmWidth * b.smmHeight * kSmmLayers * stack;
+    uint8_t *map = b.smm + out * mapBytes;
+    int32_t *marks = b.smmMarks + out * kSmmMarkRow * stack;
+    smm_paint(map, marks, stack, 0);
+    if (afterStep)
+        for (int i = 0; i < (stack - 1) * kSmmMarkRow; i++) marks[i] = marks[i + kSmmMarkRow];
+    int32_t *newest = marks + (stack - 1) * kSmmMarkRow;
+    newest[0] = smm_frame_marks(v, newest + 1, b.smmWidth, b.smmHeight);
+    if (!afterStep)
+        for (int i = 0; i < (stack - 1) * kSmmMarkRow; i++) marks[i] = newest[i % kSmmMarkRow];
+    smm_paint(map, marks, stack, 255);
+    if (finished) {
+        uint8_t *finalMap = b.finalSmm + out * mapBytes;
+        int32_t *finalMarks = b.finalSmmMarks + out * kSmmMarkRow * stack;
+        smm_paint(finalMap, finalMarks, stack, 0);
+        for (int i = 0; i < stack * kSmmMarkRow; i++) finalMarks[i] = marks[i];
+        smm_paint(finalMap, finalMarks, stack, 255);
+    }
+}
+
 /// batch_core.h:366 (WriteAgentOutputs) for simple115: one lane, one agent. A step that ends an
 /// episode also writes final_simple115.
 CB_HDNI void write_agent_outputs(const Batch &b, int e, int agent, bool afterStep) {
@@ -676,6 +746,7 @@ CB_HDNI void write_agent_outputs(const Batch &b, int e, int agent, bool afterSte
         if (finished)
             for (int i = 0; i < width; i++) b.finalSimple115[out * width + i] = st[i];
     }
+    if (b.observation & kObsSmm) write_agent_smm(b, out, v, afterStep, finished);
 }
 
 // One agent per lane.

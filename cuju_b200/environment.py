@@ -21,7 +21,7 @@ import torch
 
 from . import _native
 
-_REPRESENTATIONS = {'simple115': 1, 'simple115v2': 2}
+_REPRESENTATIONS = {'simple115': 1, 'simple115v2': 2, 'extracted': 4}
 _ACTION_SETS = {'default': 0, 'v2': 1, 'full': 2}
 _ACTION_COUNTS = {0: 19, 1: 20, 2: 33}
 
@@ -213,8 +213,12 @@ class BatchEnvironment:
             bundle_of = [0] * environment_count if assignment is None else [int(x) for x in assignment]
             values = (ctypes.c_float * (2 * environment_count))(*[v for b in bundle_of for v in per_bundle[b]])
             self._check(self._library.cuju_environment_set_difficulty(handle, values))
-        width = 115 * (4 if stacked else 1)
-        self._observation_shape = (environment_count, self.agents, width)
+        stack = 4 if stacked else 1
+        self._smm = representation == 'extracted'
+        if self._smm:
+            self._observation_shape = (environment_count, self.agents, 72, 96, 4 * stack)
+        else:
+            self._observation_shape = (environment_count, self.agents, 115 * stack)
         self._views = {}
 
     # -- plumbing ------------------------------------------------------------------------------
@@ -237,8 +241,12 @@ class BatchEnvironment:
 
     def _outputs(self):
         e, a = self.environment_count, self.agents
-        obs = self._view('simple115', self._observation_shape, '<f4', torch.float32)
-        final = self._view('final_simple115', self._observation_shape, '<f4', torch.float32)
+        if self._smm:
+            obs = self._view('smm', self._observation_shape, '|u1', torch.uint8)
+            final = self._view('final_smm', self._observation_shape, '|u1', torch.uint8)
+        else:
+            obs = self._view('simple115', self._observation_shape, '<f4', torch.float32)
+            final = self._view('final_simple115', self._observation_shape, '<f4', torch.float32)
         reward = self._view('reward', (e, a), '<f4', torch.float32)
         done = self._view('done', (e,), '|b1', torch.bool)
         score = self._view('score_reward', (e,), '<i4', torch.int32)

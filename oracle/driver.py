@@ -59,6 +59,7 @@ class OracleBatch:
         self.agents = self.lib.cuju_environment_agents(self.handle, None, None)
         self.checkpoints = checkpoints
         self.width = 115 * stack
+        self.representation = representation
         if difficulty is not None:
             values = (ctypes.c_float * (2 * environment_count))(*difficulty)
             if self.lib.cuju_environment_set_difficulty(self.handle, values) != 0:
@@ -73,8 +74,11 @@ class OracleBatch:
 
     def outputs(self):
         e, a = self.count, self.agents
-        return (self._buffer('simple115', 4 * e * a * self.width), self._buffer('reward', 4 * e * a),
-                self._buffer('done', e), self._buffer('score_reward', 4 * e))
+        if self.representation == 4:
+            obs = self._buffer('smm', e * a * 72 * 96 * 4 * (self.width // 115))
+        else:
+            obs = self._buffer('simple115', 4 * e * a * self.width)
+        return (obs, self._buffer('reward', 4 * e * a), self._buffer('done', e), self._buffer('score_reward', 4 * e))
 
     def reset(self, seeds=None):
         arr = None if seeds is None else (ctypes.c_uint * self.count)(*seeds)

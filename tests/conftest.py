@@ -80,8 +80,9 @@ def oracle_digest(assets, steps, seed=7, environments=4, **options):
     paths, counts = resolve(assets)
     checkpoints = 'checkpoints' in options.get('rewards', '')
     stack = 4 if options.get('stacked') else 1
+    representation = {'simple115': 1, 'simple115v2': 2, 'extracted': 4}[options.get('representation', 'simple115v2')]
     batch = OracleBatch(paths, counts, environments, seed, ANIMATIONS, checkpoints=checkpoints, stack=stack,
-                        assignment=options.get('assignment'))
+                        assignment=options.get('assignment'), representation=representation)
     digest = hashlib.sha256()
     digest.update(batch.reset()[0])
     for step in range(steps):
@@ -103,7 +104,8 @@ def oracle_digest(assets, steps, seed=7, environments=4, **options):
 def simple115_cases():
     """The golden cases of the representations this backend writes."""
     cases = golden()['cases']
-    return sorted(name for name, case in cases.items() if case['options'].get('representation') in (None, 'simple115v2', 'simple115'))
+    return sorted(name for name, case in cases.items()
+                  if case['options'].get('representation') in (None, 'simple115v2', 'simple115', 'extracted'))
 
 
 needs_data = pytest.mark.skipif(not os.path.isfile(ANIMATIONS), reason='run __graft_entry__.build() to stage the data')
