@@ -99,6 +99,8 @@ def declare(library: ctypes.CDLL) -> ctypes.CDLL:
     library.cuju_environment_get_state.argtypes = [p, i, ctypes.POINTER(ctypes.c_ulonglong), p]
     library.cuju_environment_set_state.argtypes = [p, i, p, ctypes.c_ulonglong, p]
     library.cuju_environment_set_stack.argtypes = [p, i, s, p, ctypes.c_ulonglong]
+    library.cuju_environment_raw_field.restype = s
+    library.cuju_environment_raw_field.argtypes = [p, i, p, p, p]
     library.cuju_environment_buffer.restype = p
     library.cuju_environment_buffer.argtypes = [p, s]
     library.cuju_environment_episode.argtypes = [p, i, p, p]

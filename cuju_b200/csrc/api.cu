@@ -86,6 +86,36 @@ struct Config {
     void *allocatorContext = nullptr;
 };
 
+// batch_core.h:121 (MakeRawLayout): the shape of each raw array after the agent axis, and its
+// place in one buffer (each array starting at a multiple of 256 bytes).
+inline RawLayout make_raw_layout(size_t outputs, int players, int sticky) {
+    RawLayout lay{};
+    lay.players = players;
+    int shape[kRawFields][3] = {{kRawF32, 3, 0}, {kRawF32, 3, 0}, {kRawF32, 3, 0}, {kRawI32, 0, 0}, {kRawI32, 0, 0}};
+    const int team[6][3] = {{kRawF32, players, 2}, {kRawF32, players, 2}, {kRawF32, players, 0},
+                            {kRawBool, players, 0}, {kRawBool, players, 0}, {kRawI32, players, 0}};
+    for (int t = 0; t < 2; t++)
+        for (int f = 0; f < 6; f++)
+            for (int k = 0; k < 3; k++) shape[kRawLeftTeam + 6 * t + f][k] = team[f][k];
+    const int tail[6][3] = {{kRawI32, 2, 0}, {kRawI32, 0, 0}, {kRawI32, 0, 0},
+                            {kRawI32, 0, 0}, {kRawI32, 0, 0}, {kRawU8, sticky, 0}};
+    for (int f = 0; f < 6; f++)
+        for (int k = 0; k < 3; k++) shape[kRawScore + f][k] = tail[f][k];
+    uint64_t offset = 0;
+    for (int f = 0; f < kRawFields; f++) {
+        RawArray &a = lay.arrays[f];
+        a.type = shape[f][0];
+        a.dims[0] = shape[f][1];
+        a.dims[1] = shape[f][2];
+        a.elements = (a.dims[0] ? a.dims[0] : 1) * (a.dims[1] ? a.dims[1] : 1);
+        a.offset = offset;
+        const int size = a.type == kRawF32 || a.type == kRawI32 ? 4 : 1;
+        offset += (outputs * a.elements * size + 255) / 256 * 256;
+    }
+    lay.bytes = offset;
+    return lay;
+}
+
 class BatchEnv {
 public:
     Allocator mem;
@@ -127,10 +157,8 @@ public:
         mem.context = c.allocatorContext;
         if ((c.observation & kObsSimple115) && (c.observation & kObsSimple115v2))
             throw std::invalid_argument("simple115 and simple115v2 are exclusive");
-        if (c.observation & kObsRaw)
-            throw std::invalid_argument("this backend writes the simple115 and extracted (SMM) representations only");
-        if (!(c.observation & (kObsSimple115 | kObsSimple115v2 | kObsSmm)))
-            throw std::invalid_argument("expected the simple115, simple115v2 or extracted representation");
+        if (!(c.observation & (kObsSimple115 | kObsSimple115v2 | kObsSmm | kObsRaw)))
+            throw std::invalid_argument("expected the simple115, simple115v2, extracted or raw representation");
         if ((c.observation & kObsSmm) &&
             (c.smmWidth < 1 || c.smmHeight < 1 || c.smmWidth > 4096 || c.smmHeight > 4096))
             throw std::invalid_argument("expected SMM dimensions from 1 to 4096, found " + std::to_string(c.smmWidth) +
@@ -244,6 +272,11 @@ public:
         }
         b.smmWidth = c.smmWidth;
         b.smmHeight = c.smmHeight;
+        if (c.observation & kObsRaw) {
+            b.rawLayout = make_raw_layout((size_t)c.count * agents, players, sticky_count(c.actionSet));
+            b.raw = alloc<uint8_t>(b.rawLayout.bytes);
+            b.finalRaw = alloc<uint8_t>(b.rawLayout.bytes);
+        }
         if (c.observation & kObsSmm) {
             // Zero maps and no marks: the first write paints onto a clear map.
             const size_t map = (size_t)c.smmWidth * c.smmHeight * kSmmLayers * c.stack;
@@ -791,12 +824,29 @@ void *cuju_environment_buffer(void *env, const char *name) {
     if (n == "final_simple115") return b.finalSimple115;
     if (n == "smm") return b.smm;
     if (n == "final_smm") return b.finalSmm;
+    if (n == "raw") return b.raw;
+    if (n == "final_raw") return b.finalRaw;
     if (n == "reward") return b.reward;
     if (n == "done") return b.done;
     if (n == "score_reward") return b.scoreReward;
     return nullptr;
 }
-const char *cuju_environment_raw_field(void *, int, int *, int *, unsigned long long *) { return nullptr; }
+const char *cuju_environment_raw_field(void *env, int field, int *type, int *dimensions, unsigned long long *offset) {
+    static const char *const names[cb::kRawFields] = {
+        "ball", "ball_direction", "ball_rotation", "ball_owned_team", "ball_owned_player", "left_team",
+        "left_team_direction", "left_team_tired_factor", "left_team_yellow_card", "left_team_active",
+        "left_team_roles", "right_team", "right_team_direction", "right_team_tired_factor",
+        "right_team_yellow_card", "right_team_active", "right_team_roles", "score", "steps_left", "game_mode",
+        "active", "designated", "sticky_actions"};
+    const cb::Batch &b = static_cast<BatchEnv *>(env)->b;
+    if (!b.raw || field < 0 || field >= cb::kRawFields) return nullptr;
+    const cb::RawArray &a = b.rawLayout.arrays[field];
+    *type = a.type;
+    dimensions[0] = a.dims[0];
+    dimensions[1] = a.dims[1];
+    *offset = a.offset;
+    return names[field];
+}
 int cuju_environment_episode(void *env, int index, long long *values, float *difficulty) {
     try {
         BatchEnv *e = static_cast<BatchEnv *>(env);

@@ -550,6 +550,25 @@ constexpr int kSimple115 = 115;
 constexpr int kSmmLayers = 4;
 constexpr int kSmmMarks = 2 * kTeamPlayers + 2;  // every player, the ball, the active player
 constexpr int kSmmMarkRow = 1 + kSmmMarks;       // a frame's mark count, then its marks
+// GRF's raw observation as separate arrays (batch_core.h:53-210): one array per field, each
+// [count][agents][dims...], every array starting at a multiple of 256 bytes of one buffer. The
+// field order and names are GRF's observation keys, so readers can index by name.
+enum RawField {
+    kRawBall, kRawBallDirection, kRawBallRotation, kRawBallOwnedTeam, kRawBallOwnedPlayer,
+    kRawLeftTeam, kRawLeftTeamDirection, kRawLeftTeamTired, kRawLeftTeamYellow, kRawLeftTeamActive, kRawLeftTeamRoles,
+    kRawRightTeam, kRawRightTeamDirection, kRawRightTeamTired, kRawRightTeamYellow, kRawRightTeamActive,
+    kRawRightTeamRoles, kRawScore, kRawStepsLeft, kRawGameMode, kRawActive, kRawDesignated, kRawSticky, kRawFields
+};
+enum RawType { kRawF32 = 0, kRawI32 = 1, kRawBool = 2, kRawU8 = 3 };
+struct RawArray {
+    int32_t type, dims[2], elements;  // dims after the agent axis, 0 when absent
+    uint64_t offset;                  // bytes into the raw buffer
+};
+struct RawLayout {
+    int32_t players;  // each team array's length: the larger team of any bundle
+    RawArray arrays[kRawFields];
+    uint64_t bytes;
+};
 
 // Per-environment books (batch_core.h:343 EnvironmentSlot).
 struct EnvSlot {
@@ -590,6 +609,8 @@ struct Batch {
     uint8_t *smm, *finalSmm;            // [count][agents][smmHeight][smmWidth][4 * stack], or null
     int32_t *smmMarks, *finalSmmMarks;  // [count][agents][stack][kSmmMarkRow]: each frame's marks
     int smmWidth, smmHeight;
+    uint8_t *raw, *finalRaw;            // the raw arrays of `rawLayout`, or null
+    RawLayout rawLayout;
     float *reward;                      // [count][agents]
     uint8_t *done;                      // [count]
     int32_t *scoreReward;               // [count]
@@ -720,6 +741,50 @@ CB_HDNI void write_agent_smm(const Batch &b, size_t out, const AgentView &v, boo
     }
 }
 
+/// batch_core.h:162 (WriteRaw): one agent's view into every raw array; team arrays shorter than
+/// the layout's players pad with zeros.
+CB_HDNI void write_agent_raw(const RawLayout &lay, uint8_t *buf, size_t out, const AgentView &v, int stepsLeft) {
+    auto at = [&](int field, int index) {
+        const RawArray &a = lay.arrays[field];
+        const int size = a.type == kRawF32 || a.type == kRawI32 ? 4 : 1;
+        return buf + a.offset + ((size_t)out * a.elements + index) * size;
+    };
+    auto f32 = [&](int field, int index, float x) { memcpy(at(field, index), &x, 4); };
+    auto i32 = [&](int field, int index, int32_t x) { memcpy(at(field, index), &x, 4); };
+    auto u8 = [&](int field, int index, int x) { *at(field, index) = (uint8_t)x; };
+    const Observation &o = v.o;
+    for (int k = 0; k < 3; k++) {
+        f32(kRawBall, k, o.ball[k]);
+        f32(kRawBallDirection, k, o.ballDirection[k]);
+        f32(kRawBallRotation, k, o.ballRotation[k]);
+    }
+    i32(kRawBallOwnedTeam, 0, o.ballOwnedTeam);
+    i32(kRawBallOwnedPlayer, 0, o.ballOwnedPlayer);
+    for (int t = 0; t < 2; t++) {
+        const TeamObs &team = o.team[t];
+        const int base = t == 0 ? kRawLeftTeam : kRawRightTeam;
+        for (int p = 0; p < lay.players; p++) {
+            const bool here = p < team.count;
+            const PlayerObs &po = team.players[here ? p : 0];
+            for (int c = 0; c < 2; c++) {
+                f32(base, 2 * p + c, here ? po.position[c] : 0.0f);
+                f32(base + 1, 2 * p + c, here ? po.direction[c] : 0.0f);
+            }
+            f32(base + 2, p, here ? po.tiredFactor : 0.0f);
+            u8(base + 3, p, here && po.yellowCard);
+            u8(base + 4, p, here && po.active);
+            i32(base + 5, p, here ? po.role : 0);
+        }
+    }
+    i32(kRawScore, 0, o.score[0]);
+    i32(kRawScore, 1, o.score[1]);
+    i32(kRawStepsLeft, 0, stepsLeft);
+    i32(kRawGameMode, 0, o.gameMode);
+    i32(kRawActive, 0, v.active);
+    i32(kRawDesignated, 0, v.designated);
+    for (int i = 0; i < lay.arrays[kRawSticky].elements; i++) u8(kRawSticky, i, i < v.stickyCount ? v.sticky[i] : 0);
+}
+
 /// batch_core.h:366 (WriteAgentOutputs) for simple115: one lane, one agent. A step that ends an
 /// episode also writes final_simple115.
 CB_HDNI void write_agent_outputs(const Batch &b, int e, int agent, bool afterStep) {
@@ -747,6 +812,11 @@ CB_HDNI void write_agent_outputs(const Batch &b, int e, int agent, bool afterSte
             for (int i = 0; i < width; i++) b.finalSimple115[out * width + i] = st[i];
     }
     if (b.observation & kObsSmm) write_agent_smm(b, out, v, afterStep, finished);
+    if (b.observation & kObsRaw) {
+        const int stepsLeft = b.worlds[e].scenario.gameDuration - v.o.step;
+        write_agent_raw(b.rawLayout, b.raw, out, v, stepsLeft);
+        if (finished) write_agent_raw(b.rawLayout, b.finalRaw, out, v, stepsLeft);
+    }
 }
 
 // One agent per lane.

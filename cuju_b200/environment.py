@@ -21,7 +21,8 @@ import torch
 
 from . import _native
 
-_REPRESENTATIONS = {'simple115': 1, 'simple115v2': 2, 'extracted': 4}
+_REPRESENTATIONS = {'simple115': 1, 'simple115v2': 2, 'extracted': 4, 'raw': 8}
+_RAW_TYPES = {0: ('<f4', torch.float32), 1: ('<i4', torch.int32), 2: ('|b1', torch.bool), 3: ('|u1', torch.uint8)}
 _ACTION_SETS = {'default': 0, 'v2': 1, 'full': 2}
 _ACTION_COUNTS = {0: 19, 1: 20, 2: 33}
 
@@ -214,6 +215,7 @@ class BatchEnvironment:
             values = (ctypes.c_float * (2 * environment_count))(*[v for b in bundle_of for v in per_bundle[b]])
             self._check(self._library.cuju_environment_set_difficulty(handle, values))
         stack = 4 if stacked else 1
+        self._raw = representation == 'raw'
         self._smm = representation == 'extracted'
         if self._smm:
             self._observation_shape = (environment_count, self.agents, 72, 96, 4 * stack)
@@ -239,9 +241,32 @@ class BatchEnvironment:
             self._views[name] = torch.as_tensor(_DeviceArray(pointer, shape, typestr), device=self._torch_device)
         return self._views[name]
 
+    def _raw_arrays(self, buffer: str) -> dict[str, torch.Tensor]:
+        """GRF's raw observation as a dict of arrays [environments, agents, ...] over `buffer`."""
+        key = ('raw-dict', buffer)
+        if key not in self._views:
+            base = self._library.cuju_environment_buffer(self._handle, buffer.encode())
+            if not base:
+                raise LibraryError(f'the batch has no buffer {buffer}')
+            arrays = {}
+            kind, dims, offset = ctypes.c_int(), (ctypes.c_int * 2)(), ctypes.c_ulonglong()
+            for field in range(64):
+                name = self._library.cuju_environment_raw_field(
+                    self._handle, field, ctypes.byref(kind), dims, ctypes.byref(offset))
+                if not name:
+                    break
+                typestr, dtype = _RAW_TYPES[kind.value]
+                shape = (self.environment_count, self.agents) + tuple(d for d in dims if d)
+                arrays[name.decode()] = torch.as_tensor(
+                    _DeviceArray(base + offset.value, shape, typestr), device=self._torch_device)
+            self._views[key] = arrays
+        return self._views[key]
+
     def _outputs(self):
         e, a = self.environment_count, self.agents
-        if self._smm:
+        if self._raw:
+            obs, final = self._raw_arrays('raw'), self._raw_arrays('final_raw')
+        elif self._smm:
             obs = self._view('smm', self._observation_shape, '|u1', torch.uint8)
             final = self._view('final_smm', self._observation_shape, '|u1', torch.uint8)
         else:
@@ -250,7 +275,7 @@ class BatchEnvironment:
         reward = self._view('reward', (e, a), '<f4', torch.float32)
         done = self._view('done', (e,), '|b1', torch.bool)
         score = self._view('score_reward', (e,), '<i4', torch.int32)
-        if self.squeeze and a == 1:
+        if self.squeeze and a == 1 and not self._raw:
             obs, final, reward = obs.squeeze(1), final.squeeze(1), reward.squeeze(1)
         return obs, reward, done, final, score
 

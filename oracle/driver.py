@@ -72,9 +72,29 @@ class OracleBatch:
     def _buffer(self, name, nbytes):
         return ctypes.string_at(self.lib.cuju_environment_buffer(self.handle, name.encode()), nbytes)
 
+    def _raw_bytes(self, name):
+        # Every raw array's bytes, the arrays in name order (as the reference's digest reads them).
+        self.lib.cuju_environment_raw_field.restype = ctypes.c_char_p
+        self.lib.cuju_environment_raw_field.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                                        ctypes.c_void_p, ctypes.c_void_p]
+        base = self.lib.cuju_environment_buffer(self.handle, name.encode())
+        kind, dims, offset = ctypes.c_int(), (ctypes.c_int * 2)(), ctypes.c_ulonglong()
+        arrays = {}
+        for field in range(64):
+            field_name = self.lib.cuju_environment_raw_field(self.handle, field, ctypes.byref(kind), dims,
+                                                             ctypes.byref(offset))
+            if not field_name:
+                break
+            elements = (dims[0] or 1) * (dims[1] or 1)
+            size = 4 if kind.value in (0, 1) else 1
+            arrays[field_name.decode()] = ctypes.string_at(base + offset.value, self.count * self.agents * elements * size)
+        return b''.join(arrays[k] for k in sorted(arrays))
+
     def outputs(self):
         e, a = self.count, self.agents
-        if self.representation == 4:
+        if self.representation == 8:
+            obs = self._raw_bytes('raw')
+        elif self.representation == 4:
             obs = self._buffer('smm', e * a * 72 * 96 * 4 * (self.width // 115))
         else:
             obs = self._buffer('simple115', 4 * e * a * self.width)

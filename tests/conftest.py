@@ -46,6 +46,10 @@ def resolve(assets):
 
 
 def tensor_bytes(tensor):
+    """The bytes of an observation; a dict of arrays (the raw representation) in name order, as
+    the reference's digest reads it."""
+    if isinstance(tensor, dict):
+        return b''.join(tensor_bytes(tensor[name]) for name in sorted(tensor))
     tensor = tensor.detach().to('cpu').contiguous()
     return tensor.numpy().tobytes()
 
@@ -80,7 +84,7 @@ def oracle_digest(assets, steps, seed=7, environments=4, **options):
     paths, counts = resolve(assets)
     checkpoints = 'checkpoints' in options.get('rewards', '')
     stack = 4 if options.get('stacked') else 1
-    representation = {'simple115': 1, 'simple115v2': 2, 'extracted': 4}[options.get('representation', 'simple115v2')]
+    representation = {'simple115': 1, 'simple115v2': 2, 'extracted': 4, 'raw': 8}[options.get('representation', 'simple115v2')]
     batch = OracleBatch(paths, counts, environments, seed, ANIMATIONS, checkpoints=checkpoints, stack=stack,
                         assignment=options.get('assignment'), representation=representation)
     digest = hashlib.sha256()
@@ -105,7 +109,7 @@ def simple115_cases():
     """The golden cases of the representations this backend writes."""
     cases = golden()['cases']
     return sorted(name for name, case in cases.items()
-                  if case['options'].get('representation') in (None, 'simple115v2', 'simple115', 'extracted'))
+                  if case['options'].get('representation') in (None, 'simple115v2', 'simple115', 'extracted', 'raw'))
 
 
 needs_data = pytest.mark.skipif(not os.path.isfile(ANIMATIONS), reason='run __graft_entry__.build() to stage the data')

@@ -83,7 +83,7 @@ def test_asset_names_resolve_to_bundles_and_agent_counts():
 # The oracle (the reference CPU backend built from source) reproduces the reference's published
 # digests: the pin of every parity test. A sample that runs in seconds; the rest run on the GPU box.
 ORACLE_CASES = ['5_vs_5/simple115v2', 'academy_empty_goal_close/simple115v2', '1_vs_1_easy/simple115v2',
-                'mixed', '11_vs_11_stochastic/checkpoints', '5_vs_5/stacked', '5_vs_5/extracted']
+                'mixed', '11_vs_11_stochastic/checkpoints', '5_vs_5/stacked', '5_vs_5/extracted', '5_vs_5/raw']
 
 
 @needs_data
