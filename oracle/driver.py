@@ -32,11 +32,12 @@ class OracleBatch:
 
     def __init__(self, bundle_paths, agent_counts, environment_count, seed, animations, threads=1,
                  representation=2, checkpoints=False, stack=1, assignment=None, difficulty=None,
-                 auto_reset=True, ticks_per_step=10, first_index=0):
-        if not os.path.isfile(LIBRARY):
-            raise RuntimeError(f'the oracle library is missing at {LIBRARY}; run make -C oracle')
+                 auto_reset=True, ticks_per_step=10, first_index=0, library=None):
+        path = library or LIBRARY
+        if not os.path.isfile(path):
+            raise RuntimeError(f'the oracle library is missing at {path}; run make -C oracle')
         native = _configuration_type()
-        self.lib = native.declare(ctypes.CDLL(LIBRARY))
+        self.lib = native.declare(ctypes.CDLL(path))
         if self.lib.cuju_backend().decode() != 'cpu':
             raise RuntimeError('expected the reference CPU backend')
         self._paths = [p.encode() for p in bundle_paths]

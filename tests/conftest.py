@@ -74,8 +74,9 @@ def device_digest(assets, steps, seed=7, environments=4, **options):
     return digest.hexdigest()
 
 
-def oracle_digest(assets, steps, seed=7, environments=4, **options):
-    """The same digest from the reference CPU backend (oracle/_ref/libcuju_cpu.so)."""
+def oracle_digest(assets, steps, seed=7, environments=4, library=None, **options):
+    """The same digest from the reference CPU backend (oracle/_ref/libcuju_cpu.so), or from another
+    library with its C-ABI that runs on the host (`library`)."""
     import struct
 
     from cuju_b200.environment import pickle_episode
@@ -86,7 +87,7 @@ def oracle_digest(assets, steps, seed=7, environments=4, **options):
     stack = 4 if options.get('stacked') else 1
     representation = {'simple115': 1, 'simple115v2': 2, 'extracted': 4, 'raw': 8}[options.get('representation', 'simple115v2')]
     batch = OracleBatch(paths, counts, environments, seed, ANIMATIONS, checkpoints=checkpoints, stack=stack,
-                        assignment=options.get('assignment'), representation=representation)
+                        assignment=options.get('assignment'), representation=representation, library=library)
     digest = hashlib.sha256()
     digest.update(batch.reset()[0])
     for step in range(steps):

@@ -1,0 +1,60 @@
+// Test infrastructure, not part of the library: the library's C-ABI (api.cu) and simulation
+// headers compiled for the host, with host memory standing in for device memory and each kernel
+// replaced by a serial loop over the environments. It lets CPU-only tests run long golden matches
+// through the same simulation source the kernels compile, at host speed. Built by
+// tests/test_host_long.py into a temporary directory; nothing in the product loads it.
+#include <cuda_runtime.h>
+#include <cstdlib>
+#include <cstring>
+#include <cstdio>
+
+static cudaError_t hs_malloc(void **p, size_t n) { *p = aligned_alloc(256, (n + 255) & ~(size_t)255); if (*p) memset(*p, 0, (n + 255) & ~(size_t)255); return *p ? cudaSuccess : cudaErrorMemoryAllocation; }
+static cudaError_t hs_memset(void *p, int v, size_t n) { memset(p, v, n); return cudaSuccess; }
+static cudaError_t hs_free(void *p) { free(p); return cudaSuccess; }
+static cudaError_t hs_memcpy(void *d, const void *s, size_t n, cudaMemcpyKind) { memmove(d, s, n); return cudaSuccess; }
+static cudaError_t hs_memcpy_async(void *d, const void *s, size_t n, cudaMemcpyKind, cudaStream_t) { memmove(d, s, n); return cudaSuccess; }
+static cudaError_t hs_ok0() { return cudaSuccess; }
+static cudaError_t hs_ok1(cudaStream_t) { return cudaSuccess; }
+static cudaError_t hs_get_limit(size_t *v, cudaLimit) { *v = 0; return cudaSuccess; }
+static cudaError_t hs_set_limit(cudaLimit, size_t) { return cudaSuccess; }
+static cudaError_t hs_get_device(int *d) { *d = 0; return cudaSuccess; }
+#define cudaMalloc(p, n) hs_malloc((void **)(p), n)
+#define cudaMemset hs_memset
+#define cudaFree hs_free
+#define cudaMemcpy hs_memcpy
+#define cudaMemcpyAsync hs_memcpy_async
+#define cudaDeviceSynchronize hs_ok0
+#define cudaStreamSynchronize hs_ok1
+#define cudaDeviceGetLimit hs_get_limit
+#define cudaDeviceSetLimit hs_set_limit
+#define cudaGetDevice hs_get_device
+#define cuju_backend cuju_backend_product
+#include "api.cu"
+#undef cuju_backend
+
+namespace cb {
+cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t) {
+    for (int e = 0; e < b.count; e++) {
+        if (b.status[e]) continue;
+        step_environment(b, e, actions);
+        if (b.status[e] && !*b.anyFail) { *b.anyFail = b.status[e]; fprintf(stderr, "env %d failed %d\n", e, b.status[e]); }
+    }
+    return cudaSuccess;
+}
+cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse, cudaStream_t) {
+    for (int e = 0; e < b.count; e++) {
+        if (mask && !mask[e]) continue;
+        if (b.status[e]) continue;
+        reset_and_write(b, e, seeds, reverse);
+        if (b.status[e] && !*b.anyFail) { *b.anyFail = b.status[e]; fprintf(stderr, "env %d failed %d\n", e, b.status[e]); }
+    }
+    return cudaSuccess;
+}
+cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t) {
+    for (int e = 0; e < b.count; e++) if (!mask || mask[e]) write_env_outputs(b, e, false);
+    return cudaSuccess;
+}
+cudaError_t kernel_attributes(size_t *l, int *r) { *l = 0; *r = 0; return cudaSuccess; }
+cudaError_t static_scratch_address(WarpScratch **out) { *out = nullptr; return cudaErrorNotSupported; }
+}
+extern "C" __attribute__((visibility("default"))) const char *cuju_backend() { return "cpu"; }

@@ -1,0 +1,41 @@
+"""The simulation source compiled for the host against the reference's long golden digests.
+
+tests/host/hostsim.cu builds the library's C-ABI and simulation headers for the host, each kernel
+replaced by a serial loop over the environments (test infrastructure; the product has no host
+path). Run through the same digest as the reference's tests, it must reproduce the long cases of
+digests.json: two full 3,010-step 11v11 matches (simple115v2, and raw), a full 5v5 match with the
+checkpoint reward, and 1,500-2,000 steps of academy drills over many episodes (extracted, and
+checkpoints). The device kernels compile the same source; the GPU tests pin them on shorter runs.
+"""
+
+import os
+import shutil
+import subprocess
+
+import pytest
+
+from conftest import ROOT, golden, needs_data, oracle_digest
+
+HOST_SOURCE = os.path.join(ROOT, 'tests', 'host', 'hostsim.cu')
+CSRC = os.path.join(ROOT, 'cuju_b200', 'csrc')
+
+
+@pytest.fixture(scope='module')
+def host_library(tmp_path_factory):
+    nvcc = shutil.which('nvcc') or '/usr/local/cuda/bin/nvcc'
+    if not os.path.isfile(nvcc):
+        pytest.skip('nvcc is needed to build the host harness')
+    out = str(tmp_path_factory.mktemp('hostsim') / 'libhostsim.so')
+    subprocess.run([nvcc, '-std=c++17', '-O2', '--fmad=false', '-prec-div=true', '-prec-sqrt=true', '-ftz=false',
+                    '-Xcompiler', '-ffp-contract=off,-fPIC,-fvisibility=hidden', '-I', CSRC, '-shared',
+                    HOST_SOURCE, '-o', out], check=True, capture_output=True)
+    return out
+
+
+@needs_data
+@pytest.mark.parametrize('case', sorted(golden()['long_cases']))
+def test_long_golden_digest_on_the_host(host_library, case):
+    g = golden()
+    entry = g['long_cases'][case]
+    assert oracle_digest(entry['assets'], entry['steps'], seed=g['seed'], environments=g['environments'],
+                         library=host_library, **entry['options']) == entry['digest']
