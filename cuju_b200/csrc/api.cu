@@ -566,13 +566,20 @@ public:
             unstarted--;
         }
     }
-    // stacked_state.h:23 (SetStackedFrames), simple115 only: the observation stack of environment
-    // `e` after set_state, `[agents][115 * stack]` float32, the oldest frame first.
+    // stacked_state.h:23 (SetStackedFrames): the observation stack of environment `e` after
+    // set_state, the oldest frame first: `[agents][115 * stack]` float32 for simple115, or
+    // `[agents][height][width][4 * stack]` uint8 for smm, whose frames must hold only 0 and 255
+    // (at most kSmmMarks cells of 255 a frame); their marks are rebuilt so that the next step
+    // clears exactly the marked bytes.
     void set_stack(int e, const std::string &name, const void *frames, size_t size) {
         check_env(e);
         if (b.stack < 2) throw std::invalid_argument("expected a batch that stacks its observations");
+        if (name == "smm" && b.smm) {
+            set_smm_stack(e, static_cast<const uint8_t *>(frames), size);
+            return;
+        }
         if (name != "simple115" || !b.simple115)
-            throw std::invalid_argument("expected the stack simple115 of the batch, found " + name);
+            throw std::invalid_argument("expected the stack simple115 or smm of the batch, found " + name);
         const size_t agents = (size_t)(hostSlots[e].leftAgents + hostSlots[e].rightAgents);
         const size_t width = (size_t)kSimple115 * b.stack;
         const size_t expected = agents * width * sizeof(float);
@@ -582,6 +589,37 @@ public:
                                         std::to_string(size));
         check(cudaDeviceSynchronize(), "set_stack");
         check(cudaMemcpy(b.simple115 + (size_t)e * b.agents * width, frames, size, cudaMemcpyHostToDevice), "set_stack");
+    }
+    void set_smm_stack(int e, const uint8_t *bytes, size_t size) {
+        const size_t agents = (size_t)(hostSlots[e].leftAgents + hostSlots[e].rightAgents);
+        const int stack = b.stack;
+        const size_t frameBytes = (size_t)b.smmWidth * b.smmHeight * kSmmLayers;
+        const size_t agentBytes = frameBytes * stack;
+        if (size != agents * agentBytes)
+            throw std::invalid_argument("expected a stack of " + std::to_string(agents * agentBytes) +
+                                        " bytes for the agents of environment " + std::to_string(e) + ", found " +
+                                        std::to_string(size));
+        std::vector<int32_t> marks(agents * stack * kSmmMarkRow, 0);
+        for (size_t a = 0; a < agents; a++)
+            for (int f = 0; f < stack; f++) {
+                int32_t *row = marks.data() + (a * stack + f) * kSmmMarkRow;
+                for (size_t m = 0; m < frameBytes; m++) {
+                    const uint8_t v = bytes[a * agentBytes + m / kSmmLayers * kSmmLayers * stack + kSmmLayers * f +
+                                            m % kSmmLayers];
+                    if (v == 0) continue;
+                    if (v != 255 || row[0] == kSmmMarks)
+                        throw std::invalid_argument("expected a minimap of GRF, of at most " + std::to_string(kSmmMarks) +
+                                                    " cells of 255 a frame and zeros, found a cell of " +
+                                                    std::to_string(v));
+                    row[1 + row[0]++] = (int32_t)m;
+                }
+            }
+        check(cudaDeviceSynchronize(), "set_stack");
+        const size_t first = (size_t)e * b.agents;
+        check(cudaMemcpy(b.smm + first * agentBytes, bytes, size, cudaMemcpyHostToDevice), "set_stack");
+        check(cudaMemcpy(b.smmMarks + first * kSmmMarkRow * stack, marks.data(), marks.size() * sizeof(int32_t),
+                         cudaMemcpyHostToDevice),
+              "set_stack");
     }
     std::string get_state(int e, EnvCore &core, EnvSlot &slot) {
         check_env(e);
