@@ -110,3 +110,38 @@ def test_episode_pickle_reads_back():
 
     assert unpickle_episode(pickle_episode([0, 0, -1], None), 2) == [0, 0, -1, 0, 0]
     assert unpickle_episode(pickle_episode([2, 3, 1], [0, 4, 1, 0]), 4) == [2, 3, 1, 0, 4, 1, 0]
+
+
+@needs_data
+@pytest.mark.skipif(not os.path.isfile(LIBRARY), reason='library not built')
+def test_memory_estimate_without_a_device():
+    """cuju_memory_estimate plans the batch's buffers without touching a GPU: linear in the
+    environments, and the SMM and raw representations add exactly their buffers (up to the
+    256-byte rounding of each allocation)."""
+    from conftest import ANIMATIONS, resolve
+    from cuju_b200 import _native
+
+    library = _native.declare(ctypes.CDLL(LIBRARY))
+    paths, counts = resolve('11_vs_11_stochastic_l1_r0')
+    keep = []
+
+    def estimate(envs, observation=2):
+        p = (ctypes.c_char_p * 1)(paths[0].encode())
+        c = (ctypes.c_int * 2)(*counts[0])
+        keep.extend([p, c])
+        config = _native.Configuration(version=2, assets=p, asset_count=1, animations=ANIMATIONS.encode(),
+                                       environment_count=envs, seed=0, observation=observation, auto_reset=1,
+                                       ticks_per_step=10, smm_width=96, smm_height=72, stack=1,
+                                       agent_counts=ctypes.cast(c, ctypes.c_void_p))
+        out = ctypes.c_ulonglong()
+        assert library.cuju_memory_estimate(ctypes.byref(config), ctypes.byref(out)) == 0, library.cuju_last_error()
+        return out.value
+
+    slack = 64 * 256
+    step = estimate(32) - estimate(16)
+    assert step > 16 * 370_000
+    assert abs((estimate(48) - estimate(32)) - step) <= slack
+    # One agent: the SMM map and its final copy (72 x 96 x 4 bytes each), two mark rows of 25
+    # int32, in place of the two simple115 buffers (115 float32 each).
+    smm = 2 * 72 * 96 * 4 + 2 * 25 * 4 - 2 * 115 * 4
+    assert abs((estimate(16, 4) - estimate(16)) - 16 * smm) <= slack
