@@ -64,7 +64,7 @@ EXPORTED = (
     'cuju_environment_synchronize', 'cuju_environment_get_state', 'cuju_environment_set_state',
     'cuju_environment_set_stack', 'cuju_environment_buffer', 'cuju_environment_raw_field',
     'cuju_environment_episode', 'cuju_environment_scenario', 'cuju_state_layout',
-    'cuju_state_gather',
+    'cuju_state_gather', 'cuju_state_padding',
 )
 
 

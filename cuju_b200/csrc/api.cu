@@ -948,11 +948,27 @@ int cuju_b200_kernel_info(unsigned long long *out) {
     }
 }
 
-int cuju_state_layout(void) {
-    lastError = "state layouts are not available in this backend";
-    return -1;
+int cuju_state_padding(const char *bytes, unsigned long long size, unsigned char *mask) {
+    try {
+        if (!bytes || !mask) throw std::invalid_argument("expected the bytes of a match and a mask");
+        cb::host::Codec codec;
+        std::vector<size_t> positions;
+        if (!codec.padding(std::string(bytes, size), positions))
+            throw std::invalid_argument("expected the bytes of a match");
+        memset(mask, 0, size);
+        for (size_t p : positions) mask[p] = 1;
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
 }
-int cuju_state_gather(void) {
+const char *cuju_state_layout(unsigned long long *size) {
+    if (size) *size = 0;
+    lastError = "state layouts are not available in this backend";
+    return nullptr;
+}
+int cuju_state_gather(const char *, unsigned long long, int, const unsigned long long *, const unsigned int *, int,
+                      unsigned char *) {
     lastError = "state gathers are not available in this backend";
     return -1;
 }

@@ -11,6 +11,8 @@
 #include <cstdlib>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
+#include <memory>
 #include <vector>
 
 #include "match_util.cuh"
@@ -43,9 +45,11 @@ struct Archive {
     std::string bytes;
     size_t off = 0;
     std::vector<LoadedPointer> *pointers = nullptr;
+    std::vector<size_t> *radians = nullptr;  // byte positions of the angles, when recorded
 
     template <class T>
     void f(T &v) {
+        if (std::is_same<T, Radian>::value && radians) radians->push_back(off);
         if (load) {
             if (off + sizeof(T) > bytes.size()) throw std::runtime_error("state too short");
             memcpy(&v, bytes.data() + off, sizeof(T));
@@ -227,6 +231,24 @@ struct Codec {
         Archive a{false, std::string()};
         process_state(a, w, freeControllerCount);
         return a.bytes;
+    }
+    // state_api.h:21 (cuju_state_padding): GRF saves an angle as its float, its flag and three
+    // bytes of padding that hold whatever its memory held; the positions of those bytes in the
+    // match bytes, so that two states can be compared without them. Empty if the bytes hold no
+    // match.
+    bool padding(const std::string &bytes, std::vector<size_t> &positions) {
+        std::unique_ptr<Match> w(new Match);
+        if (!load(bytes, *w)) return false;
+        std::vector<size_t> radians;
+        Archive a{true, bytes};
+        a.radians = &radians;
+        clear_match(*w);
+        process_state(a, *w, freeControllerCount);
+        positions.clear();
+        for (size_t r : radians)
+            if (r + 8 <= bytes.size())
+                for (size_t k = 5; k < 8; k++) positions.push_back(r + k);
+        return true;
     }
     // Bytes to a world in the rest frame (mirror 0), as StateCodec::LoadFrame.
     bool load_frame(const std::string &bytes, Match &w) {

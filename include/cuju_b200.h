@@ -104,9 +104,13 @@ int cuju_b200_kernel_info(unsigned long long *out);
  * Returns 0, or -1 with the reason in cuju_last_error (more than 32 environments, host or foreign
  * actions, a batch not yet reset, a CUDA error). */
 int cuju_b200_environment_step_static(void *environment, const int *actions, void *stream);
-/* src/state_api.h (state field layout and gather); this backend reports them unavailable */
-int cuju_state_layout(void);
-int cuju_state_gather(void);
+/* state_api.h:21; 1 in `mask` at the padding bytes GRF saves uninitialized, 0 elsewhere */
+int cuju_state_padding(const char *bytes, unsigned long long size, unsigned char *mask);
+/* state_api.h:51 and :86 (the reference's in-memory state layout and a gather over it); this
+ * backend's state lies differently in memory, so it returns null and -1 with a message */
+const char *cuju_state_layout(unsigned long long *size);
+int cuju_state_gather(const char *bytes, unsigned long long size, int frame, const unsigned long long *offsets,
+                      const unsigned int *sizes, int count, unsigned char *out);
 
 #ifdef __cplusplus
 }

@@ -145,3 +145,37 @@ def test_memory_estimate_without_a_device():
     # int32, in place of the two simple115 buffers (115 float32 each).
     smm = 2 * 72 * 96 * 4 + 2 * 25 * 4 - 2 * 115 * 4
     assert abs((estimate(16, 4) - estimate(16)) - 16 * smm) <= slack
+
+
+@needs_data
+@pytest.mark.skipif(not (os.path.isfile(LIBRARY) and os.path.isfile(ORACLE)), reason='library or oracle not built')
+@pytest.mark.parametrize('assets', ['11_vs_11_stochastic_l1_r0', '5_vs_5_l4_r0', 'academy_corner_l1_r0'])
+def test_state_padding_equals_the_reference(assets):
+    """cuju_state_padding marks the same padding bytes of a state as the reference's (state_api.h:21),
+    without a device: the angles' three uninitialized bytes."""
+    import random
+
+    from conftest import ANIMATIONS, resolve
+    from oracle.driver import OracleBatch
+
+    paths, counts = resolve(assets)
+    batch = OracleBatch(paths, counts, 2, 5, ANIMATIONS, threads=1)
+    ours = ctypes.CDLL(LIBRARY)
+    try:
+        batch.reset()
+        rng = random.Random(2)
+        for _ in range(20):
+            batch.step([rng.randrange(19) for _ in range(2 * batch.agents)])
+        data, _ = batch.engine_state(1)
+        masks = []
+        for library in (ours, batch.lib):
+            library.cuju_state_padding.argtypes = [ctypes.c_char_p, ctypes.c_ulonglong, ctypes.c_void_p]
+            mask = (ctypes.c_ubyte * len(data))()
+            assert library.cuju_state_padding(data, len(data), mask) == 0
+            masks.append(bytes(mask))
+        assert masks[0] == masks[1]
+        assert sum(masks[0]) > 0
+        bad = (ctypes.c_ubyte * 4)()
+        assert ours.cuju_state_padding(b'\x00\x01', 2, bad) == -1
+    finally:
+        batch.close()
