@@ -32,7 +32,8 @@ class OracleBatch:
 
     def __init__(self, bundle_paths, agent_counts, environment_count, seed, animations, threads=1,
                  representation=2, checkpoints=False, stack=1, assignment=None, difficulty=None,
-                 auto_reset=True, ticks_per_step=10, first_index=0, library=None):
+                 auto_reset=True, ticks_per_step=10, first_index=0, library=None, fixed_seeds=None,
+                 episode_number=0):
         path = library or LIBRARY
         if not os.path.isfile(path):
             raise RuntimeError(f'the oracle library is missing at {path}; run make -C oracle')
@@ -44,14 +45,15 @@ class OracleBatch:
         paths = (ctypes.c_char_p * len(self._paths))(*self._paths)
         counts = (ctypes.c_int * (2 * len(self._paths)))(*[c for pair in agent_counts for c in pair])
         assign = None if assignment is None else (ctypes.c_int * environment_count)(*assignment)
+        self._fixed = None if fixed_seeds is None else (ctypes.c_longlong * environment_count)(*fixed_seeds)
         config = native.Configuration(
             version=2, assets=paths, asset_count=len(self._paths),
             assignment=ctypes.cast(assign, ctypes.c_void_p) if assign else None,
             animations=animations.encode(), environment_count=environment_count, seed=seed,
             action_set=0, observation=representation, checkpoints=int(checkpoints), numpy_legacy=1,
             auto_reset=int(auto_reset), threads=threads, ticks_per_step=ticks_per_step, smm_width=96, smm_height=72,
-            stack=stack, fixed_seeds=None, agent_counts=ctypes.cast(counts, ctypes.c_void_p),
-            episode_number=0, first_index=first_index, allocate=None, release=None, allocator_context=None,
+            stack=stack, fixed_seeds=ctypes.cast(self._fixed, ctypes.c_void_p) if self._fixed else None,
+            agent_counts=ctypes.cast(counts, ctypes.c_void_p), episode_number=episode_number, first_index=first_index, allocate=None, release=None, allocator_context=None,
             pin_threads=0, numa=0, page_aligned=0)
         self.handle = self.lib.cuju_environment_create(ctypes.byref(config))
         if not self.handle:
@@ -101,10 +103,17 @@ class OracleBatch:
             obs = self._buffer('simple115', 4 * e * a * self.width)
         return (obs, self._buffer('reward', 4 * e * a), self._buffer('done', e), self._buffer('score_reward', 4 * e))
 
-    def reset(self, seeds=None):
+    def reset(self, seeds=None, reverse=None):
         arr = None if seeds is None else (ctypes.c_uint * self.count)(*seeds)
-        self._check(self.lib.cuju_environment_reset(self.handle, arr, None, None))
+        rev = None if reverse is None else (ctypes.c_int * self.count)(*reverse)
+        self._check(self.lib.cuju_environment_reset(self.handle, arr, rev, None))
         return self.outputs()
+
+    def step_status(self, actions):
+        # The step's return code (0, -1, or -2 for a host action out of range) and its message.
+        arr = (ctypes.c_int * (self.count * self.agents))(*actions)
+        rc = self.lib.cuju_environment_step(self.handle, arr, 0, None, 1)
+        return rc, (self.lib.cuju_last_error() or b'').decode() if rc else ''
 
     def reset_masked(self, mask, seeds=None):
         m = (ctypes.c_ubyte * self.count)(*mask)

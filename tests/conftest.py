@@ -114,3 +114,21 @@ def simple115_cases():
 
 
 needs_data = pytest.mark.skipif(not os.path.isfile(ANIMATIONS), reason='run __graft_entry__.build() to stage the data')
+
+
+@pytest.fixture(scope='session')
+def host_library(tmp_path_factory):
+    """The library built for the host from tests/host/hostsim.cu (test infrastructure: the C-ABI and
+    the simulation source with host memory and a serial loop in place of each kernel)."""
+    import shutil
+    import subprocess
+
+    nvcc = shutil.which('nvcc') or '/usr/local/cuda/bin/nvcc'
+    if not os.path.isfile(nvcc):
+        pytest.skip('nvcc is needed to build the host harness')
+    out = str(tmp_path_factory.mktemp('hostsim') / 'libhostsim.so')
+    subprocess.run([nvcc, '-std=c++17', '-O2', '--fmad=false', '-prec-div=true', '-prec-sqrt=true', '-ftz=false',
+                    '-Xcompiler', '-ffp-contract=off,-fPIC,-fvisibility=hidden',
+                    '-I', os.path.join(ROOT, 'cuju_b200', 'csrc'), '-shared',
+                    os.path.join(ROOT, 'tests', 'host', 'hostsim.cu'), '-o', out], check=True, capture_output=True)
+    return out

@@ -1,0 +1,85 @@
+"""The C-ABI's batch options on the host build (tests/host/hostsim.cu) against the reference CPU
+backend: fixed seeds with GRF's episode number over many automatic restarts, team order given
+at reset, masked resets with given and drawn seeds, first_index, and host actions out of range
+(-2) or negative (counted from the end). Every output buffer is compared after every call, and the
+state bytes at the end. These are the host-side paths of api.cu and env.cuh that the device
+kernels share; the GPU tests cover the device build on shorter runs.
+"""
+
+import random
+
+import pytest
+
+from conftest import ANIMATIONS, needs_data, resolve
+
+pytestmark = [needs_data]
+
+
+def _pair(host_library, assets, envs, seed, **options):
+    from oracle.driver import OracleBatch
+
+    paths, counts = resolve(assets)
+    return [OracleBatch(paths, counts, envs, seed, ANIMATIONS, threads=1, library=library, **options)
+            for library in (None, host_library)]
+
+
+def _run(batches, steps, rng, masked=False, agents_actions=19):
+    ref, mine = batches
+    envs = ref.count
+    for step in range(steps):
+        acts = [rng.randrange(agents_actions) for _ in range(envs * ref.agents)]
+        assert mine.step(acts) == ref.step(acts), f'step {step} differs'
+        if masked and rng.random() < 0.3:
+            mask = [1 if rng.random() < 0.3 else 0 for _ in range(envs)]
+            seeds = [rng.randrange(0, 2**32) if rng.random() < 0.5 else -1 for _ in range(envs)]
+            assert mine.reset_masked(mask, seeds) == ref.reset_masked(mask, seeds), f'masked reset {step} differs'
+    for index in range(envs):
+        assert mine.engine_state(index) == ref.engine_state(index), f'state {index} differs'
+
+
+def test_fixed_seeds_and_episode_number_over_many_episodes(host_library):
+    batches = _pair(host_library, 'academy_empty_goal_close_l1_r0', 6, 3, fixed_seeds=[5, -1, 7, -1, 11, 11],
+                    episode_number=3, checkpoints=True)
+    try:
+        assert batches[1].reset() == batches[0].reset()
+        _run(batches, 300, random.Random(1))
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_reverse_at_reset_and_first_index(host_library):
+    batches = _pair(host_library, '5_vs_5_l4_r0', 4, 9, first_index=1000)
+    try:
+        reverse = [1, 0, 1, 0]
+        assert batches[1].reset([4, 4, 8, 8], reverse) == batches[0].reset([4, 4, 8, 8], reverse)
+        _run(batches, 40, random.Random(2))
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_masked_resets_with_given_and_drawn_seeds(host_library):
+    batches = _pair(host_library, '11_vs_11_easy_stochastic_l1_r0', 6, 4, difficulty=[0.3, -1.0] * 6)
+    try:
+        assert batches[1].reset() == batches[0].reset()
+        _run(batches, 40, random.Random(3), masked=True)
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_host_actions_out_of_range_and_negative(host_library):
+    batches = _pair(host_library, '5_vs_5_l4_r0', 2, 1)
+    ref, mine = batches
+    try:
+        assert mine.reset() == ref.reset()
+        n = ref.agents * 2
+        for acts in ([-1] * n, [-19] * n, [18] * n):
+            assert mine.step(acts) == ref.step(acts)
+        for acts in ([19] * n, [-20] * n):
+            r, m = ref.step_status(acts), mine.step_status(acts)
+            assert r[0] == m[0] == -2, (r, m)
+    finally:
+        for b in batches:
+            b.close()

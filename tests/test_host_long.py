@@ -8,28 +8,9 @@ checkpoint reward, and 1,500-2,000 steps of academy drills over many episodes (e
 checkpoints). The device kernels compile the same source; the GPU tests pin them on shorter runs.
 """
 
-import os
-import shutil
-import subprocess
-
 import pytest
 
-from conftest import ROOT, golden, needs_data, oracle_digest
-
-HOST_SOURCE = os.path.join(ROOT, 'tests', 'host', 'hostsim.cu')
-CSRC = os.path.join(ROOT, 'cuju_b200', 'csrc')
-
-
-@pytest.fixture(scope='module')
-def host_library(tmp_path_factory):
-    nvcc = shutil.which('nvcc') or '/usr/local/cuda/bin/nvcc'
-    if not os.path.isfile(nvcc):
-        pytest.skip('nvcc is needed to build the host harness')
-    out = str(tmp_path_factory.mktemp('hostsim') / 'libhostsim.so')
-    subprocess.run([nvcc, '-std=c++17', '-O2', '--fmad=false', '-prec-div=true', '-prec-sqrt=true', '-ftz=false',
-                    '-Xcompiler', '-ffp-contract=off,-fPIC,-fvisibility=hidden', '-I', CSRC, '-shared',
-                    HOST_SOURCE, '-o', out], check=True, capture_output=True)
-    return out
+from conftest import golden, needs_data, oracle_digest
 
 
 @needs_data
