@@ -33,7 +33,7 @@ class OracleBatch:
     def __init__(self, bundle_paths, agent_counts, environment_count, seed, animations, threads=1,
                  representation=2, checkpoints=False, stack=1, assignment=None, difficulty=None,
                  auto_reset=True, ticks_per_step=10, first_index=0, library=None, fixed_seeds=None,
-                 episode_number=0):
+                 episode_number=0, action_set=0, numpy_legacy=True):
         path = library or LIBRARY
         if not os.path.isfile(path):
             raise RuntimeError(f'the oracle library is missing at {path}; run make -C oracle')
@@ -50,7 +50,8 @@ class OracleBatch:
             version=2, assets=paths, asset_count=len(self._paths),
             assignment=ctypes.cast(assign, ctypes.c_void_p) if assign else None,
             animations=animations.encode(), environment_count=environment_count, seed=seed,
-            action_set=0, observation=representation, checkpoints=int(checkpoints), numpy_legacy=1,
+            action_set=action_set, observation=representation, checkpoints=int(checkpoints),
+            numpy_legacy=int(numpy_legacy),
             auto_reset=int(auto_reset), threads=threads, ticks_per_step=ticks_per_step, smm_width=96, smm_height=72,
             stack=stack, fixed_seeds=ctypes.cast(self._fixed, ctypes.c_void_p) if self._fixed else None,
             agent_counts=ctypes.cast(counts, ctypes.c_void_p), episode_number=episode_number, first_index=first_index, allocate=None, release=None, allocator_context=None,

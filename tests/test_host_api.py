@@ -1,7 +1,8 @@
 """The C-ABI's batch options on the host build (tests/host/hostsim.cu) against the reference CPU
 backend: fixed seeds with GRF's episode number over many automatic restarts, team order given
-at reset, masked resets with given and drawn seeds, first_index, and host actions out of range
-(-2) or negative (counted from the end). Every output buffer is compared after every call, and the
+at reset, masked resets with given and drawn seeds, first_index, host actions out of range (-2)
+or negative (counted from the end), the v2 and full action sets, checkpoint rewards without the
+NumPy-legacy rounding, and other tick counts per step. Every output buffer is compared after every call, and the
 state bytes at the end. These are the host-side paths of api.cu and env.cuh that the device
 kernels share; the GPU tests cover the device build on shorter runs.
 """
@@ -80,6 +81,38 @@ def test_host_actions_out_of_range_and_negative(host_library):
         for acts in ([19] * n, [-20] * n):
             r, m = ref.step_status(acts), mine.step_status(acts)
             assert r[0] == m[0] == -2, (r, m)
+    finally:
+        for b in batches:
+            b.close()
+
+
+@pytest.mark.parametrize('action_set,actions', [(1, 20), (2, 33)])
+def test_other_action_sets(host_library, action_set, actions):
+    batches = _pair(host_library, '5_vs_5_l4_r0', 3, 6, action_set=action_set)
+    try:
+        assert batches[1].reset() == batches[0].reset()
+        _run(batches, 60, random.Random(4), agents_actions=actions)
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_checkpoint_rewards_without_the_numpy_legacy_rounding(host_library):
+    batches = _pair(host_library, 'academy_counterattack_easy_l1_r0', 4, 8, checkpoints=True, numpy_legacy=False)
+    try:
+        assert batches[1].reset() == batches[0].reset()
+        _run(batches, 200, random.Random(5))
+    finally:
+        for b in batches:
+            b.close()
+
+
+@pytest.mark.parametrize('ticks', [1, 4])
+def test_other_ticks_per_step(host_library, ticks):
+    batches = _pair(host_library, '11_vs_11_stochastic_l1_r0', 2, 2, ticks_per_step=ticks)
+    try:
+        assert batches[1].reset() == batches[0].reset()
+        _run(batches, 40, random.Random(6))
     finally:
         for b in batches:
             b.close()
