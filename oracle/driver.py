@@ -110,6 +110,10 @@ class OracleBatch:
         self._check(self.lib.cuju_environment_reset(self.handle, arr, rev, None))
         return self.outputs()
 
+    def reset_done(self):
+        self._check(self.lib.cuju_environment_reset_done(self.handle, None))
+        return self.outputs()
+
     def step_status(self, actions):
         # The step's return code (0, -1, or -2 for a host action out of range) and its message.
         arr = (ctypes.c_int * (self.count * self.agents))(*actions)

@@ -116,3 +116,27 @@ def test_other_ticks_per_step(host_library, ticks):
     finally:
         for b in batches:
             b.close()
+
+
+def test_episodes_without_automatic_restart(host_library):
+    """auto_reset off: an ended environment keeps its outputs (reward and score zeroed while done)
+    until reset_done starts its next episode."""
+    batches = _pair(host_library, 'academy_empty_goal_close_l1_r0', 4, 12, auto_reset=False)
+    ref, mine = batches
+    rng = random.Random(7)
+    try:
+        assert mine.reset() == ref.reset()
+        restarts = 0
+        for step in range(250):
+            acts = [rng.randrange(19) for _ in range(4 * ref.agents)]
+            out = ref.step(acts)
+            assert mine.step(acts) == out, f'step {step} differs'
+            if any(out[2]) and rng.random() < 0.5:
+                assert mine.reset_done() == ref.reset_done(), f'reset_done at {step} differs'
+                restarts += 1
+        assert restarts > 0
+        for index in range(4):
+            assert mine.engine_state(index) == ref.engine_state(index)
+    finally:
+        for b in batches:
+            b.close()
