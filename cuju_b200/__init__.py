@@ -5,5 +5,7 @@ reference's `cuju_*` entry points, and `BatchEnvironment` mirrors the reference 
 """
 
 from .environment import ActionRangeError, BatchEnvironment, LibraryError, bundled_assets, resolve_asset
+from .multi_device import EpisodeTotals, MultiDeviceBatch
 
-__all__ = ['ActionRangeError', 'BatchEnvironment', 'LibraryError', 'bundled_assets', 'resolve_asset']
+__all__ = ['ActionRangeError', 'BatchEnvironment', 'EpisodeTotals', 'LibraryError', 'MultiDeviceBatch',
+           'bundled_assets', 'resolve_asset']

@@ -91,6 +91,9 @@ def declare(library: ctypes.CDLL) -> ctypes.CDLL:
     library.cuju_environment_reset.argtypes = [p, p, p, p]
     library.cuju_environment_reset_masked.argtypes = [p, p, i, p, p, p, i]
     library.cuju_environment_reset_done.argtypes = [p, p]
+    # This build's own extension; the reference libraries that the same declarations serve lack it.
+    if hasattr(library, 'cuju_b200_environment_reset_masked_device'):
+        library.cuju_b200_environment_reset_masked_device.argtypes = [p, p, p, p]
     library.cuju_environment_step.argtypes = [p, p, i, p, i]
     library.cuju_environment_step_async.argtypes = [p, p, i, p]
     library.cuju_environment_step_wait.argtypes = [p]

@@ -423,6 +423,20 @@ public:
         check(launch_reset(b, md, sd, rd, stream), "reset launch");
         if (mask && !onDevice) check(cudaStreamSynchronize(stream), "host mask");
     }
+    // Masked reset with the mask and seeds already in device memory: nothing is read back or
+    // checked on the host and nothing synchronises, so the call can sit in a captured graph beside
+    // the step. The started books need the mask on the host, so a device mask is refused until
+    // every environment has started (a reset without a mask starts them all).
+    void reset_masked_device(const uint8_t *mask, const int64_t *seeds, cudaStream_t stream) {
+        if (mask && unstarted > 0)
+            throw std::logic_error("expected every environment started (a reset of the whole batch) before a "
+                                   "masked reset with a device mask");
+        check(launch_reset(b, mask, seeds, nullptr, stream), "reset launch");
+        if (!mask && unstarted > 0) {
+            started.assign(b.count, true);
+            unstarted = 0;
+        }
+    }
     void step(const int32_t *actions, bool onDevice, cudaStream_t stream, bool synchronize) {
         check_started();
         const int32_t *ad = actions;
@@ -766,6 +780,17 @@ int cuju_environment_reset_masked(void *env, const unsigned char *mask, int mask
         BatchEnv *e = static_cast<BatchEnv *>(env);
         e->reset_masked(mask, mask_on_device != 0, seeds, reverse, as_stream(stream));
         if (synchronize) e->sync(as_stream(stream));
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
+}
+// No reference counterpart: see include/cuju_b200.h.
+int cuju_b200_environment_reset_masked_device(void *env, const unsigned char *mask, const long long *seeds,
+                                              void *stream) {
+    try {
+        static_cast<BatchEnv *>(env)->reset_masked_device(mask, reinterpret_cast<const int64_t *>(seeds),
+                                                          as_stream(stream));
         return 0;
     } catch (const std::exception &e) {
         return fail(e);

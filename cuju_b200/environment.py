@@ -281,8 +281,16 @@ class BatchEnvironment:
 
     # -- the environment API -------------------------------------------------------------------
     def reset(self, seeds: Any = None, reverse: Any = None, mask: Any = None) -> torch.Tensor:
-        """Starts the next episode of every environment (or of those `mask` selects)."""
+        """Starts the next episode of every environment (or of those `mask` selects).
+
+        Seeds given as a CUDA tensor take the device path (`cuju_b200_environment_reset_masked_device`):
+        the mask, if any, must be a CUDA tensor too, nothing is read back to the host and nothing
+        synchronises, so the reset can follow a step inside one captured graph. A negative device
+        seed draws the next seed, as -1 does; the device path takes no `reverse`.
+        """
         e = self.environment_count
+        if isinstance(seeds, torch.Tensor) and seeds.is_cuda:
+            return self._reset_device(seeds, mask, reverse)
         seed_t = None if seeds is None else torch.as_tensor(seeds, dtype=torch.int64).reshape(-1).expand(e).contiguous()
         rev_t = None if reverse is None else torch.as_tensor(reverse, dtype=torch.int32).reshape(-1).expand(e).contiguous()
         if seed_t is not None and bool(((seed_t < -1) | (seed_t > 4294967295)).any()):
@@ -304,6 +312,21 @@ class BatchEnvironment:
                     self._handle, seeds32, None if rev_t is None else rev_t.data_ptr(), self._stream()))
         return self._outputs()[0]
 
+    def _reset_device(self, seeds: torch.Tensor, mask: Any, reverse: Any) -> torch.Tensor:
+        e = self.environment_count
+        if reverse is not None:
+            raise ValueError('a reset with device seeds takes no reverse flags')
+        if mask is not None and not (isinstance(mask, torch.Tensor) and mask.is_cuda):
+            raise ValueError('a reset with device seeds takes its mask on a CUDA device too')
+        seed_t = seeds.to(self._torch_device, torch.int64).reshape(-1).expand(e).contiguous()
+        mask_t = None if mask is None else mask.to(self._torch_device, torch.uint8).reshape(-1).expand(e).contiguous()
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_b200_environment_reset_masked_device(
+                self._handle, None if mask_t is None else mask_t.data_ptr(), seed_t.data_ptr(), self._stream()))
+        # The reset reads the staged tensors on the stream; keep them alive until it has run.
+        self._device_reset_inputs = (seed_t, mask_t)
+        return self._outputs()[0]
+
     def reset_done(self) -> None:
         """Starts the next episode of every environment whose episode ended (auto_reset off)."""
         with torch.cuda.device(self._torch_device):
@@ -321,6 +344,30 @@ class BatchEnvironment:
                 self._handle, a.data_ptr(), int(a.is_cuda), self._stream(), int(synchronize)))
         obs, reward, done, final, score = self._outputs()
         return obs, reward, done, {'final_observation': final, 'score_reward': score}
+
+    def step_async(self, actions: Any) -> None:
+        """Starts one step of every environment on the current stream and returns at once (host
+        actions are copied before it returns); `step_wait` gives the outputs."""
+        a = torch.as_tensor(actions)
+        if a.dim() == 1:
+            a = a.reshape(self.environment_count, -1)
+        a = a.to(torch.int32).contiguous()
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_step_async(
+                self._handle, a.data_ptr(), int(a.is_cuda), self._stream()))
+        self._async_actions = a
+
+    def step_wait(self):
+        """Waits for the step `step_async` started and returns what `step` returns."""
+        self._check(self._library.cuju_environment_step_wait(self._handle))
+        self.synchronize()
+        self._async_actions = None
+        obs, reward, done, final, score = self._outputs()
+        return obs, reward, done, {'final_observation': final, 'score_reward': score}
+
+    def observation(self):
+        """The observation of every agent that the last reset or step wrote."""
+        return self._outputs()[0]
 
     def synchronize(self) -> None:
         with torch.cuda.device(self._torch_device):

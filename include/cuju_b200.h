@@ -104,6 +104,17 @@ int cuju_b200_kernel_info(unsigned long long *out);
  * Returns 0, or -1 with the reason in cuju_last_error (more than 32 environments, host or foreign
  * actions, a batch not yet reset, a CUDA error). */
 int cuju_b200_environment_step_static(void *environment, const int *actions, void *stream);
+/* No reference counterpart (the reference takes masked-reset seeds from the host only,
+ * environment_api.h:263-271). A masked reset whose `mask` (uint8 [environments], nonzero = reset;
+ * null = every environment) and `seeds` (int64 [environments]; negative draws the next seed of the
+ * environment's generator, as -1 does in cuju_environment_reset_masked, and a value of 2^32 or
+ * more keeps its low 32 bits; null = draw every seed) are both in device memory of the current
+ * device. Nothing is checked or read on the host and nothing synchronises: the reset runs on
+ * `stream` after the work before it, so a step and this reset can be captured in one CUDA graph.
+ * A non-null `mask` is refused until every environment has started. Returns 0, or -1 with the
+ * reason in cuju_last_error. */
+int cuju_b200_environment_reset_masked_device(void *environment, const unsigned char *mask, const long long *seeds,
+                                              void *stream);
 /* state_api.h:21; 1 in `mask` at the padding bytes GRF saves uninitialized, 0 elsewhere */
 int cuju_state_padding(const char *bytes, unsigned long long size, unsigned char *mask);
 /* state_api.h:51 and :86 (the reference's in-memory state layout and a gather over it); this

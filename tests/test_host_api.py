@@ -140,3 +140,55 @@ def test_episodes_without_automatic_restart(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+def test_masked_reset_with_device_seeds(host_library):
+    """`cuju_b200_environment_reset_masked_device` (mask and seeds in device memory, no host check)
+    on the host build, where device memory is host memory, against the reference's host-seed masked
+    reset: the first call without a mask starts every environment, negative seeds draw as -1 does,
+    and a seed of 2^32 or more plays as its low 32 bits. A mask before every environment has
+    started is refused."""
+    import ctypes
+
+    batches = _pair(host_library, '5_vs_5_l4_r0', 6, 21)
+    ref, mine = batches
+    mine.lib.cuju_b200_environment_reset_masked_device.argtypes = [ctypes.c_void_p] * 4
+    device_reset = mine.lib.cuju_b200_environment_reset_masked_device
+    rng = random.Random(11)
+    try:
+        ones = (ctypes.c_ubyte * 6)(*[1] * 6)
+        assert device_reset(mine.handle, ones, None, None) == -1
+        assert b'started' in mine.lib.cuju_last_error()
+        first = [3, -1, 2**32 + 5, -7, 9, 0]
+        given = (ctypes.c_longlong * 6)(*first)
+        expected = [s & 0xffffffff if s >= 0 else -1 for s in first]
+        ref._check(ref.lib.cuju_environment_reset_masked(
+            ref.handle, None, 0, (ctypes.c_longlong * 6)(*expected), None, None, 1))
+        assert device_reset(mine.handle, None, given, None) == 0
+        assert mine.outputs() == ref.outputs()
+        for step in range(60):
+            acts = [rng.randrange(19) for _ in range(6 * ref.agents)]
+            assert mine.step(acts) == ref.step(acts), f'step {step} differs'
+            if step % 7 == 3:
+                mask = [1 if rng.random() < 0.4 else 0 for _ in range(6)]
+                seeds = [rng.choice((-1, -5, rng.randrange(2**32), 2**32 + rng.randrange(2**32))) for _ in range(6)]
+                wanted = ref.reset_masked(mask, [s & 0xffffffff if s >= 0 else -1 for s in seeds])
+                rc = device_reset(mine.handle, (ctypes.c_ubyte * 6)(*mask), (ctypes.c_longlong * 6)(*seeds), None)
+                assert rc == 0 and mine.outputs() == wanted, f'device masked reset at {step} differs'
+        for index in range(6):
+            assert mine.engine_state(index) == ref.engine_state(index)
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_drawn_seeds_with_first_index_over_restarts(host_library):
+    """A part of a larger batch (first_index 20): seeds drawn at reset and at every automatic
+    restart follow the seed rule of environments 20 onwards, as in the reference."""
+    batches = _pair(host_library, 'academy_empty_goal_close_l1_r0', 12, 5, first_index=20)
+    try:
+        assert batches[1].reset() == batches[0].reset()
+        _run(batches, 120, random.Random(13))
+    finally:
+        for b in batches:
+            b.close()
