@@ -2,8 +2,10 @@
 backend: fixed seeds with GRF's episode number over many automatic restarts, team order given
 at reset, masked resets with given and drawn seeds, first_index, host actions out of range (-2)
 or negative (counted from the end), the v2 and full action sets, checkpoint rewards without the
-NumPy-legacy rounding, and other tick counts per step. Every output buffer is compared after every call, and the
-state bytes at the end. These are the host-side paths of api.cu and env.cuh that the device
+NumPy-legacy rounding, other tick counts per step, episodes without automatic restart, the
+device-resident masked reset, and the shapes of the bench's other configurations (all 11 players
+controlled with masked resets; mixed bundles, stacked). Every output buffer is compared after every
+call, and the state bytes at the end. These are the host-side paths of api.cu and env.cuh that the device
 kernels share; the GPU tests cover the device build on shorter runs.
 """
 
@@ -189,6 +191,49 @@ def test_drawn_seeds_with_first_index_over_restarts(host_library):
     try:
         assert batches[1].reset() == batches[0].reset()
         _run(batches, 120, random.Random(13))
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_every_left_player_controlled_at_high_difficulty_with_masked_resets(host_library):
+    """The shape of the bench's 65,536-environment configuration at a testable size: 11v11 with all
+    11 left players controlled (`11_vs_11_hard_stochastic_l11_r0`, right team at 0.95), and a masked
+    reset with fresh seeds after most steps."""
+    batches = _pair(host_library, '11_vs_11_hard_stochastic_l11_r0', 4, 0, first_index=4096)
+    ref, mine = batches
+    rng = random.Random(17)
+    try:
+        assert ref.agents == 11
+        assert mine.reset() == ref.reset()
+        for step in range(40):
+            acts = [rng.randrange(19) for _ in range(4 * 11)]
+            assert mine.step(acts) == ref.step(acts), f'step {step} differs'
+            mask = [1 if rng.random() < 0.15 else 0 for _ in range(4)]
+            seeds = [rng.randrange(0, 2**32) for _ in range(4)]
+            assert mine.reset_masked(mask, seeds) == ref.reset_masked(mask, seeds), f'masked reset {step} differs'
+        for index in range(4):
+            assert mine.engine_state(index) == ref.engine_state(index)
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_mixed_bundles_interleaved_and_stacked(host_library):
+    """The shape of the bench's mixed configuration at a testable size: three bundles (11v11 with
+    one agent, 5v5 with four, a drill with one) interleaved by index with the assignment
+    [0, 1, 0, 1, 2], four-frame stacked observations, and automatic restarts."""
+    assets = ['11_vs_11_stochastic_l1_r0', '5_vs_5_l4_r0', 'academy_empty_goal_close_l1_r0']
+    assignment = [[0, 1, 0, 1, 2][i % 5] for i in range(10)]
+    batches = _pair(host_library, assets, 10, 3, assignment=assignment, stack=4)
+    ref, mine = batches
+    rng = random.Random(19)
+    try:
+        assert ref.agents == 4
+        assert mine.reset() == ref.reset()
+        for step in range(80):
+            acts = [rng.randrange(19) for _ in range(10 * 4)]
+            assert mine.step(acts) == ref.step(acts), f'step {step} differs'
     finally:
         for b in batches:
             b.close()
