@@ -237,3 +237,78 @@ def test_mixed_bundles_interleaved_and_stacked(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+def test_device_actions_outside_the_set_step_as_idle(host_library):
+    """Actions flagged as device-resident go unchecked: an index outside [-n, n) acts as idle
+    (action 0) and a negative one in range counts from the end, as batch_core.h:617-621 decodes
+    them. On the host build the device buffer is host memory, so the kernel path reads them."""
+    import ctypes
+
+    batches = _pair(host_library, '5_vs_5_l4_r0', 3, 6)
+    ref, mine = batches
+    try:
+        assert mine.reset() == ref.reset()
+        n = 3 * ref.agents
+        for bad, same in (([19, 1000, -20, -2**31] * 3, [0] * n), ([-1, -19, 5, -7] * 3, [18, 0, 5, 12] * 3)):
+            arr = (ctypes.c_int * n)(*bad)
+            assert mine.lib.cuju_environment_step(mine.handle, arr, 1, None, 1) == 0
+            assert mine.outputs() == ref.step(same)
+        for index in range(3):
+            assert mine.engine_state(index) == ref.engine_state(index)
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_state_bytes_that_stop_short_or_run_on_are_refused(host_library):
+    """set_state refuses engine bytes cut short or followed by more, as the reference does
+    (tests/test_state_errors.py), and leaves the environment as it was."""
+    import ctypes
+
+    batches = _pair(host_library, '5_vs_5_l4_r0', 2, 2)
+    ref, mine = batches
+    try:
+        assert mine.reset() == ref.reset()
+        for b in batches:
+            b.lib.cuju_environment_set_state.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p,
+                                                         ctypes.c_ulonglong, ctypes.c_void_p]
+        acts = [3] * (2 * ref.agents)
+        assert mine.step(acts) == ref.step(acts)
+        data, episode = ref.engine_state(1)
+        values = (ctypes.c_int * 25)(*episode[:25])
+        for wrong in (data[:-10], data[:len(data) // 2], data + b'\0\0\0'):
+            codes = [b.lib.cuju_environment_set_state(b.handle, 0, wrong, len(wrong), values) for b in batches]
+            assert codes == [-1, -1], f'{len(wrong)} of {len(data)} bytes: {codes}'
+        assert mine.engine_state(0) == ref.engine_state(0)
+        assert mine.step(acts) == ref.step(acts)
+    finally:
+        for b in batches:
+            b.close()
+
+
+def test_an_async_step_equals_a_step(host_library):
+    """cuju_environment_step_async followed by cuju_environment_step_wait gives what a step gives,
+    and checks host actions the same way (-2 before anything runs)."""
+    import ctypes
+
+    batches = _pair(host_library, '5_vs_5_l4_r0', 2, 12)
+    ref, mine = batches
+    rng = random.Random(23)
+    try:
+        assert mine.reset() == ref.reset()
+        n = 2 * ref.agents
+        for step in range(20):
+            acts = [rng.randrange(19) for _ in range(n)]
+            arr = (ctypes.c_int * n)(*acts)
+            assert mine.lib.cuju_environment_step_async(mine.handle, arr, 0, None) == 0
+            assert mine.lib.cuju_environment_step_wait(mine.handle) == 0
+            assert mine.outputs() == ref.step(acts), f'async step {step} differs'
+        arr = (ctypes.c_int * n)(*([19] * n))
+        assert mine.lib.cuju_environment_step_async(mine.handle, arr, 0, None) == -2
+        assert mine.lib.cuju_environment_step_wait(mine.handle) == 0
+        acts = [1] * n
+        assert mine.step(acts) == ref.step(acts)
+    finally:
+        for b in batches:
+            b.close()
