@@ -1,0 +1,30 @@
+"""Output shapes on a B200 (reference tests/test_shapes.py, test_squeeze): with `squeeze` a batch
+of one agent drops the agent axis of its observation and reward, and its values are those of the
+same batch without it."""
+
+import pytest
+import torch
+
+from conftest import needs_data
+
+pytestmark = [pytest.mark.gpu, needs_data]
+
+
+def test_squeeze_drops_the_agent_axis_of_one_agent():
+    from cuju_b200 import BatchEnvironment
+
+    plain = BatchEnvironment('academy_empty_goal_close_l1_r0', environment_count=4, seed=3)
+    squeezed = BatchEnvironment('academy_empty_goal_close_l1_r0', environment_count=4, seed=3, squeeze=True)
+    try:
+        first, second = plain.reset(), squeezed.reset()
+        assert first.shape == (4, 1, 115) and second.shape == (4, 115)
+        assert torch.equal(second, first[:, 0])
+        for step in range(5):
+            actions = torch.tensor([1, 5, 9, 13], dtype=torch.int32) + step
+            a = plain.step(actions.reshape(4, 1).cuda())
+            b = squeezed.step(actions.cuda())
+            assert b[0].shape == (4, 115) and b[1].shape == (4,) and b[2].shape == (4,)
+            assert torch.equal(b[0], a[0][:, 0]) and torch.equal(b[1], a[1][:, 0]) and torch.equal(b[2], a[2])
+    finally:
+        plain.close()
+        squeezed.close()
