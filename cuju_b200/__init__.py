@@ -4,8 +4,10 @@ A drop-in for the reference's CUDA backend: the C-ABI library `lib/libcuju_b200.
 reference's `cuju_*` entry points, and `BatchEnvironment` mirrors the reference Python class.
 """
 
-from .environment import ActionRangeError, BatchEnvironment, LibraryError, bundled_assets, resolve_asset
+from . import errors
+from .environment import BatchEnvironment, bundled_assets, resolve_asset
+from .errors import ActionRangeError, LibraryError
 from .multi_device import EpisodeTotals, MultiDeviceBatch
 
 __all__ = ['ActionRangeError', 'BatchEnvironment', 'EpisodeTotals', 'LibraryError', 'MultiDeviceBatch',
-           'bundled_assets', 'resolve_asset']
+           'bundled_assets', 'errors', 'resolve_asset']

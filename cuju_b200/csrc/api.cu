@@ -25,7 +25,7 @@ struct CudaError : std::runtime_error {
     using std::runtime_error::runtime_error;
 };
 static void check(cudaError_t rc, const char *what) {
-    if (rc != cudaSuccess) throw CudaError(std::string(what) + ": " + cudaGetErrorString(rc));
+    if (rc != cudaSuccess) throw CudaError(std::string("cuda error in ") + what + ": " + cudaGetErrorString(rc));
 }
 
 // Optional caller-provided device allocator (the reference's allocate/release callbacks).

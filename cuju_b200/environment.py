@@ -20,19 +20,13 @@ from typing import Any
 import torch
 
 from . import _native
+from .errors import (ActionRangeError, ArgumentError, ChoiceError, ClosedError, ConfigurationError, LibraryError,
+                     MissingFileError, StateError, from_library)
 
 _REPRESENTATIONS = {'simple115': 1, 'simple115v2': 2, 'extracted': 4, 'raw': 8}
 _RAW_TYPES = {0: ('<f4', torch.float32), 1: ('<i4', torch.int32), 2: ('|b1', torch.bool), 3: ('|u1', torch.uint8)}
 _ACTION_SETS = {'default': 0, 'v2': 1, 'full': 2}
 _ACTION_COUNTS = {0: 19, 1: 20, 2: 33}
-
-
-class LibraryError(RuntimeError):
-    """The library refused a call; the message is the library's."""
-
-
-class ActionRangeError(LibraryError, IndexError):
-    """A host action lies outside [-n, n) for n actions."""
 
 
 def bundled_assets() -> list[str]:
@@ -67,7 +61,7 @@ def resolve_asset(asset: str) -> tuple[str, tuple[int, int]]:
         if bases:
             base = min(bases, key=lambda n: sum(_split_name(n)[1:]))
             return os.path.join(directory, base + '.cjb'), (left, right)
-    raise FileNotFoundError(f'expected an asset bundle path or `<scenario>_l<left>_r<right>`, found {asset!r}')
+    raise MissingFileError(f'expected an asset bundle path or `<scenario>_l<left>_r<right>`, found {asset!r}')
 
 
 class _DeviceArray:
@@ -148,15 +142,15 @@ class BatchEnvironment:
         first_index: int = 0,
     ):
         if representation not in _REPRESENTATIONS:
-            raise ValueError(f'expected one of {sorted(_REPRESENTATIONS)}, found {representation!r}')
+            raise ChoiceError(f'expected one of {sorted(_REPRESENTATIONS)}, found {representation!r}')
         if action_set not in _ACTION_SETS:
-            raise ValueError(f'expected one of {sorted(_ACTION_SETS)}, found {action_set!r}')
+            raise ChoiceError(f'expected one of {sorted(_ACTION_SETS)}, found {action_set!r}')
         reward_names = [r.strip() for r in rewards.split(',') if r.strip()]
         if not reward_names or reward_names[0] != 'scoring' or not set(reward_names) <= {'scoring', 'checkpoints'}:
-            raise ValueError(f"expected 'scoring' or 'scoring,checkpoints', found {rewards!r}")
+            raise ConfigurationError(f"expected 'scoring' or 'scoring,checkpoints', found {rewards!r}")
         self._torch_device = torch.device(device)
         if self._torch_device.type != 'cuda':
-            raise ValueError('the B200 batch runs on a CUDA device only')
+            raise ChoiceError(f'expected a CUDA device (this build has no CPU backend), found {self._torch_device}')
         if self._torch_device.index is None:
             self._torch_device = torch.device('cuda', torch.cuda.current_device())
         self._library = _native.load(library)
@@ -199,8 +193,8 @@ class BatchEnvironment:
         with torch.cuda.device(self._torch_device):
             handle = self._library.cuju_environment_create(ctypes.byref(config))
         if not handle:
-            raise LibraryError(self._library.cuju_last_error().decode())
-        self._handle = handle
+            raise from_library(self._library.cuju_last_error().decode())
+        self._native_handle = handle
         self.environment_count = environment_count
         left = (ctypes.c_int * environment_count)()
         right = (ctypes.c_int * environment_count)()
@@ -228,7 +222,16 @@ class BatchEnvironment:
         if status == -2:
             raise ActionRangeError(self._library.cuju_last_error().decode())
         if status != 0:
-            raise LibraryError(self._library.cuju_last_error().decode())
+            raise from_library(self._library.cuju_last_error().decode())
+
+    @property
+    def _handle(self):
+        # Every library call goes through here, so a call after close raises instead of passing
+        # the library a null batch.
+        handle = self.__dict__.get('_native_handle')
+        if not handle:
+            raise ClosedError('the batch is closed')
+        return handle
 
     def _stream(self) -> int:
         return torch.cuda.current_stream(self._torch_device).cuda_stream
@@ -294,7 +297,7 @@ class BatchEnvironment:
         seed_t = None if seeds is None else torch.as_tensor(seeds, dtype=torch.int64).reshape(-1).expand(e).contiguous()
         rev_t = None if reverse is None else torch.as_tensor(reverse, dtype=torch.int32).reshape(-1).expand(e).contiguous()
         if seed_t is not None and bool(((seed_t < -1) | (seed_t > 4294967295)).any()):
-            raise ValueError(f'expected seeds from 0 to 4294967295, or -1 to draw, found {seed_t.tolist()}')
+            raise ArgumentError(f'expected seeds from 0 to 4294967295, or -1 to draw, found {seed_t.tolist()}')
         with torch.cuda.device(self._torch_device):
             if mask is not None or (seed_t is not None and bool((seed_t == -1).any())):
                 mask_t, on_device = None, 0
@@ -315,9 +318,9 @@ class BatchEnvironment:
     def _reset_device(self, seeds: torch.Tensor, mask: Any, reverse: Any) -> torch.Tensor:
         e = self.environment_count
         if reverse is not None:
-            raise ValueError('a reset with device seeds takes no reverse flags')
+            raise ArgumentError('a reset with device seeds takes no reverse flags')
         if mask is not None and not (isinstance(mask, torch.Tensor) and mask.is_cuda):
-            raise ValueError('a reset with device seeds takes its mask on a CUDA device too')
+            raise ArgumentError('a reset with device seeds takes its mask on a CUDA device too')
         seed_t = seeds.to(self._torch_device, torch.int64).reshape(-1).expand(e).contiguous()
         mask_t = None if mask is None else mask.to(self._torch_device, torch.uint8).reshape(-1).expand(e).contiguous()
         with torch.cuda.device(self._torch_device):
@@ -381,7 +384,7 @@ class BatchEnvironment:
         with torch.cuda.device(self._torch_device):
             pointer = self._library.cuju_environment_get_state(self._handle, index, ctypes.byref(size), episode)
         if not pointer:
-            raise LibraryError(self._library.cuju_last_error().decode())
+            raise from_library(self._library.cuju_last_error().decode())
         return ctypes.string_at(pointer, size.value), list(episode)
 
     def get_state(self, index: int) -> bytes:
@@ -398,8 +401,14 @@ class BatchEnvironment:
         values = (ctypes.c_int * (3 + _native.MAXIMUM_AGENTS))(*list(episode)[:3 + _native.MAXIMUM_AGENTS])
         torch.cuda.synchronize(self._torch_device)
         with torch.cuda.device(self._torch_device):
-            self._check(self._library.cuju_environment_set_state(
-                self._handle, index, ctypes.c_char_p(match), len(match), values))
+            status = self._library.cuju_environment_set_state(
+                self._handle, index, ctypes.c_char_p(match), len(match), values)
+        if status != 0:
+            # As the reference does: a refusal of the bytes is a StateError, a CUDA failure stays
+            # what it is.
+            message = self._library.cuju_last_error().decode()
+            error = from_library(message)
+            raise StateError(message) if type(error) is LibraryError else error
 
     def set_state(self, index: int, state: bytes) -> None:
         """Sets environment `index` from GRF's state bytes (episode pickle, then engine), as
@@ -426,11 +435,13 @@ class BatchEnvironment:
         return int(self._library.cuju_environment_memory_bytes(self._handle))
 
     def close(self) -> None:
-        if getattr(self, '_handle', None):
+        """Frees the batch; a second call does nothing, and other calls then raise ClosedError."""
+        handle = self.__dict__.get('_native_handle')
+        if handle:
             torch.cuda.synchronize(self._torch_device)
-            self._views.clear()
-            self._library.cuju_environment_destroy(self._handle)
-            self._handle = None
+            self.__dict__.get('_views', {}).clear()
+            self._native_handle = None
+            self._library.cuju_environment_destroy(handle)
 
     def __del__(self):
         try:

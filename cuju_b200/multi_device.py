@@ -20,18 +20,19 @@ from typing import Any
 import torch
 
 from .environment import BatchEnvironment
+from .errors import ArgumentError, ChoiceError, ClosedError, ConfigurationError, EnvironmentIndexError
 
 __all__ = ['EpisodeTotals', 'MultiDeviceBatch']
 
 
-def _per_environment(values, start, end, count):
+def _per_environment(values, start, end, count, error=ConfigurationError):
     """The values of environments `start` to `end - 1`, or the one value shared by every one
     (reference multi_device.py:38-49)."""
     array = torch.as_tensor(values)
     if array.dim() == 0:
         return array.item()
     if array.shape[0] != count:
-        raise ValueError(
+        raise error(
             f'expected one value, or one for each of the {count} environments, found the shape {tuple(array.shape)}')
     return array[start:end]
 
@@ -52,17 +53,17 @@ class MultiDeviceBatch:
                  game_engine_random_seed: Any = None, **options: Any) -> None:
         self.devices = [self._device(d) for d in devices]
         if not self.devices:
-            raise ValueError('expected at least one device')
+            raise ConfigurationError('expected at least one device')
         for name in ('device', 'first_index'):
             if name in options:
-                raise ValueError(f'expected no {name}, which MultiDeviceBatch sets for each part')
+                raise ConfigurationError(f'expected no {name}, which MultiDeviceBatch sets for each part')
         count = len(self.devices)
         if split is None:
             split = [environment_count // count + (part < environment_count % count) for part in range(count)]
         split = [int(size) for size in split]
         if len(split) != count or sum(split) != environment_count or min(split) < 1:
-            raise ValueError(f'expected a split of the {environment_count} environments into {count} parts of at '
-                             f'least one, found {split}')
+            raise ConfigurationError(f'expected a split of the {environment_count} environments into {count} parts '
+                                     f'of at least one, found {split}')
         self.ranges = []
         start = 0
         for size in split:
@@ -99,7 +100,7 @@ class MultiDeviceBatch:
         """A CUDA device with an index, from an index, a name or a `torch.device`."""
         device = torch.device('cuda', device) if isinstance(device, int) else torch.device(device)
         if device.type != 'cuda':
-            raise ValueError(f'expected a CUDA device (this build has no CPU backend), found {device}')
+            raise ChoiceError(f'expected a CUDA device (this build has no CPU backend), found {device}')
         if device.index is None:
             device = torch.device('cuda', torch.cuda.current_device())
         return device
@@ -117,7 +118,7 @@ class MultiDeviceBatch:
 
     def _open_parts(self):
         if not getattr(self, 'parts', None):
-            raise RuntimeError('the batch is closed')
+            raise ClosedError('the batch is closed')
         return self.parts
 
     def __reduce__(self):
@@ -141,7 +142,8 @@ class MultiDeviceBatch:
     def _split(self, values):
         if values is None:
             return [None] * len(self.parts)
-        return [_per_environment(values, start, end, self.environment_count) for start, end in self.ranges]
+        return [_per_environment(values, start, end, self.environment_count, ArgumentError)
+                for start, end in self.ranges]
 
     # -- the environment API -------------------------------------------------------------------
     def reset(self, seeds: Any = None, reverse: Any = None) -> Any:
@@ -186,7 +188,7 @@ class MultiDeviceBatch:
         for part, (start, end) in zip(self._open_parts(), self.ranges):
             if start <= index < end:
                 return part, index - start
-        raise IndexError(f'expected an environment from 0 to {self.environment_count - 1}, found {index}')
+        raise EnvironmentIndexError(f'expected an environment from 0 to {self.environment_count - 1}, found {index}')
 
     def get_state(self, index: int) -> bytes:
         part, local = self._part(index)

@@ -28,3 +28,21 @@ def test_squeeze_drops_the_agent_axis_of_one_agent():
     finally:
         plain.close()
         squeezed.close()
+
+
+def test_calls_after_close_raise_closed_error():
+    """A closed batch raises ClosedError (a RuntimeError) instead of handing the library a null
+    batch; a second close does nothing (reference tests/test_errors.py)."""
+    from cuju_b200 import BatchEnvironment
+    from cuju_b200.errors import ClosedError
+
+    batch = BatchEnvironment('academy_empty_goal_close_l1_r0', environment_count=2, seed=1)
+    batch.reset()
+    batch.close()
+    batch.close()
+    with pytest.raises(ClosedError):
+        batch.step(torch.zeros((2, 1), dtype=torch.int32))
+    with pytest.raises(ClosedError):
+        batch.get_state(0)
+    with pytest.raises(ClosedError):
+        batch.reset()

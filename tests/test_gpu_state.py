@@ -61,7 +61,7 @@ def test_set_state_matches_the_reference_cpu_backend(assets):
 
 def test_set_state_refuses_another_scenario():
     from cuju_b200 import BatchEnvironment
-    from cuju_b200.environment import LibraryError
+    from cuju_b200.errors import StateError
     from oracle.driver import OracleBatch
 
     paths, counts = resolve('5_vs_5_l4_r0')
@@ -71,7 +71,8 @@ def test_set_state_refuses_another_scenario():
         other.reset()
         mine.reset()
         data, episode = other.engine_state(0)
-        with pytest.raises(LibraryError, match='scenario of the environment'):
+        # A refused state is a StateError, as in the reference (environment.py:1611-1612).
+        with pytest.raises(StateError, match='scenario of the environment'):
             mine.set_engine_state(0, data, episode)
     finally:
         mine.close()
