@@ -98,12 +98,17 @@ CB_HD float nclamp(float v, float lo, float hi) {
     return (c - lo) / (hi - lo);
 }
 CB_HD int sign_side(float v) { return v >= 0 ? 1 : -1; }
-// One period added or removed per iteration, so each keeps its rounding.
+// One period added or removed per iteration, so each keeps its rounding. With the span of 2*pi
+// that every caller passes, the loops end for |v| below 2^27 (above it v - span rounds back to v)
+// and take at most about 18.1 million iterations there; the cap of 2^25 per loop changes no
+// result where they end, and stops them where they would not (an infinite or huge angle, which
+// GRF leaves undefined) instead of holding the launch forever.
 CB_HD float wrap_range(float lo, float hi, float v) {
+    constexpr unsigned kCap = 1u << 25;
     float span = hi - lo;
     float r = v;
-    while (r < lo) r += span;
-    while (r > hi) r -= span;
+    for (unsigned i = 0; r < lo && i < kCap; i++) r += span;
+    for (unsigned i = 0; r > hi && i < kCap; i++) r -= span;
     return r;
 }
 // A float written with printf("%f") and read back with atof, then narrowed to float: the exact

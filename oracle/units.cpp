@@ -54,3 +54,12 @@ extern "C" __attribute__((visibility("default"))) int oracle_hungarian(const int
         for (int i = 0; i < size; i++) columns[i] = cols[i];
     return total;
 }
+
+// The reference's range wrap (cuju include/cuju/math_utilities.h:33, GRF's ModulateIntoRange).
+// Callers pass only values on which its loops end (|value| below 2^27 for a span of 2*pi).
+#include "cuju/math_utilities.h"
+
+extern "C" __attribute__((visibility("default"))) float oracle_modulate_into_range(float min, float max,
+                                                                                  float value) {
+    return cuju::ModulateIntoRange(min, max, value);
+}

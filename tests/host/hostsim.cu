@@ -58,3 +58,8 @@ cudaError_t kernel_attributes(size_t *l, int *r) { *l = 0; *r = 0; return cudaSu
 cudaError_t static_scratch_address(WarpScratch **out) { *out = nullptr; return cudaErrorNotSupported; }
 }
 extern "C" __attribute__((visibility("default"))) const char *cuju_backend() { return "cpu"; }
+
+// The device code's range wrap, for a unit check against the reference's (tests/test_host_api.py).
+extern "C" __attribute__((visibility("default"))) float hostsim_wrap_range(float lo, float hi, float v) {
+    return cb::wrap_range(lo, hi, v);
+}

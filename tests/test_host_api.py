@@ -312,3 +312,44 @@ def test_an_async_step_equals_a_step(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+def test_range_wrap_equals_the_reference_and_ends_on_any_angle(host_library):
+    """The device code's range wrap (`common.cuh: wrap_range`, host build) equals the reference's
+    ModulateIntoRange bit for bit wherever the reference's loops end (|v| below 2^27 for the
+    2*pi span), and returns on the angles where those loops never end (infinities, huge values)."""
+    import ctypes
+    import math
+    import os
+    import struct
+
+    units_path = os.path.join(os.path.dirname(__file__), '..', 'oracle', '_ref', 'liboracle_units.so')
+    if not os.path.isfile(units_path):
+        pytest.skip('run make -C oracle for the unit shim')
+    units = ctypes.CDLL(units_path)
+    mine = ctypes.CDLL(host_library)
+    for fn in (units.oracle_modulate_into_range, mine.hostsim_wrap_range):
+        fn.argtypes = [ctypes.c_float] * 3
+        fn.restype = ctypes.c_float
+
+    def f32(x):
+        return struct.unpack('<f', struct.pack('<f', x))[0]
+
+    def bits(x):
+        return struct.pack('<f', x)
+
+    pi = f32(math.pi)
+    rng = random.Random(29)
+    values = [0.0, -0.0, pi, -pi, f32(pi * 1.0000001), 2 * pi, -2 * pi, 7.0, -7.0, 1e-30, 123456.7, -98765.4]
+    values += [rng.uniform(-10, 10) for _ in range(2000)]
+    values += [rng.uniform(-1e5, 1e5) for _ in range(200)]
+    values += [rng.choice((-1, 1)) * rng.uniform(1e6, 1.3e8) for _ in range(6)]
+    below = 2.0 ** 27 - 8  # the largest float below 2^27
+    values += [f32(below), -f32(below)]
+    for v in values:
+        v = f32(v)
+        assert bits(mine.hostsim_wrap_range(-pi, pi, v)) == bits(units.oracle_modulate_into_range(-pi, pi, v)), v
+    for v in (math.inf, -math.inf, 2.0 ** 28, -1e30, 3e38):
+        r = mine.hostsim_wrap_range(-pi, pi, v)
+        assert not (-pi <= r <= pi)
+    assert math.isnan(mine.hostsim_wrap_range(-pi, pi, math.nan))
