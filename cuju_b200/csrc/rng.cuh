@@ -67,14 +67,19 @@ struct MatchRng {
         return z;
     }
     // Boost uniform_real<float>: Next()/2^32 in float, redrawn when it rounds up to the maximum.
+    // A redraw happens about once in 2^25 draws for a range of [0, 1), so no match redraws 2^16
+    // times in a row; the cap only ends the loop for a stored range where no draw can fall below
+    // the maximum (equal or NaN bounds in corrupted state), which would otherwise never return.
     CB_HD float uniform() {
         const float mn = lo(), mx = hi();
-        for (;;) {
+        float r = mn;
+        for (unsigned redraws = 0; redraws < (1u << 16); redraws++) {
             float num = (float)(next() - 0u);
             float div = (float)(0xffffffffu - 0u) + 1;
-            float r = num / div * (mx - mn) + mn;
+            r = num / div * (mx - mn) + mn;
             if (r < mx) return r;
         }
+        return r;
     }
 };
 CB_HD float random_in_range(uint8_t *rngBytes, float mn, float mx) {
