@@ -353,3 +353,41 @@ def test_range_wrap_equals_the_reference_and_ends_on_any_angle(host_library):
         r = mine.hostsim_wrap_range(-pi, pi, v)
         assert not (-pi <= r <= pi)
     assert math.isnan(mine.hostsim_wrap_range(-pi, pi, math.nan))
+
+
+def test_episode_values_equal_the_reference(host_library):
+    """cuju_environment_episode (seed, team order, resets so far, episode offset, bundle, step of the
+    last observation, fixed seed, determinism, ticks, agents, players, designated players, and the
+    played and scenario difficulties) equals the reference's for every environment, after resets,
+    automatic restarts and masked resets, with mixed bundles, fixed seeds and per-side difficulty."""
+    import ctypes
+
+    assets = ['academy_empty_goal_close_l1_r0', '5_vs_5_l4_r0']
+    batches = _pair(host_library, assets, 6, 31, assignment=[0, 1, 0, 1, 0, 0],
+                    fixed_seeds=[-1, 9, -1, -1, 4, -1], episode_number=2,
+                    difficulty=[0.4, -1.0, -1.0, 0.7, 0.1, 0.2, 1.0, -1.0, -1.0, -1.0, 0.5, 0.5])
+    ref, mine = batches
+    for b in batches:
+        b.lib.cuju_environment_episode.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+
+    def episode(b, index):
+        values, difficulty = (ctypes.c_longlong * 17)(), (ctypes.c_float * 4)()
+        assert b.lib.cuju_environment_episode(b.handle, index, values, difficulty) == 0
+        return list(values), [ctypes.c_float(x).value for x in difficulty]
+
+    rng = random.Random(37)
+    try:
+        assert mine.reset() == ref.reset()
+        for step in range(90):
+            acts = [rng.randrange(19) for _ in range(6 * ref.agents)]
+            assert mine.step(acts) == ref.step(acts), f'step {step} differs'
+            if step % 15 == 7:
+                mask = [1 if rng.random() < 0.5 else 0 for _ in range(6)]
+                seeds = [rng.randrange(2**32) if rng.random() < 0.5 else -1 for _ in range(6)]
+                assert mine.reset_masked(mask, seeds) == ref.reset_masked(mask, seeds)
+            if step % 10 == 0:
+                for index in range(6):
+                    assert episode(mine, index) == episode(ref, index), f'episode {index} at {step}'
+    finally:
+        for b in batches:
+            b.close()
