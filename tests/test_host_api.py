@@ -391,3 +391,45 @@ def test_episode_values_equal_the_reference(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+def test_batch_description_equals_the_reference(host_library):
+    """The calls that describe a batch (environment count, agents and players per environment and
+    side, the difficulty each environment plays, the scenario name of each bundle, the output
+    buffers it has) answer as the reference's do for a mixed batch with per-bundle agent counts."""
+    import ctypes
+
+    assets = ['11_vs_11_stochastic_l1_r0', '5_vs_5_l4_r0', 'academy_empty_goal_close_l1_r0']
+    batches = _pair(host_library, assets, 7, 2, assignment=[2, 1, 0, 1, 2, 0, 0],
+                    difficulty=[0.3, -1.0] * 3 + [-1.0, 0.9] * 4)
+    p = ctypes.c_void_p
+    for b in batches:
+        b.lib.cuju_environment_difficulty.argtypes = [p, p]
+        b.lib.cuju_environment_difficulty.restype = None
+        b.lib.cuju_environment_scenario.argtypes = [p, ctypes.c_int]
+        b.lib.cuju_environment_scenario.restype = ctypes.c_char_p
+        b.lib.cuju_environment_buffer.argtypes = [p, ctypes.c_char_p]
+        b.lib.cuju_environment_buffer.restype = p
+
+    def describe(b):
+        out = {'count': b.lib.cuju_environment_count(b.handle)}
+        for name in ('agents', 'players'):
+            left, right = (ctypes.c_int * 7)(), (ctypes.c_int * 7)()
+            total = getattr(b.lib, f'cuju_environment_{name}')(b.handle, left, right)
+            out[name] = (total, list(left), list(right))
+        difficulty = (ctypes.c_float * 14)()
+        b.lib.cuju_environment_difficulty(b.handle, difficulty)
+        out['difficulty'] = list(difficulty)
+        out['scenarios'] = [b.lib.cuju_environment_scenario(b.handle, i) for i in range(4)]
+        out['buffers'] = {name: bool(b.lib.cuju_environment_buffer(b.handle, name))
+                          for name in (b'simple115', b'final_simple115', b'reward', b'done', b'score_reward',
+                                       b'smm', b'raw', b'no_such_buffer')}
+        return out
+
+    try:
+        assert describe(mine := batches[1]) == describe(batches[0])
+        assert mine.reset() == batches[0].reset()
+        assert describe(mine) == describe(batches[0])
+    finally:
+        for b in batches:
+            b.close()
