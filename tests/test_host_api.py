@@ -433,3 +433,45 @@ def test_batch_description_equals_the_reference(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+def test_argument_refusals_equal_the_reference(host_library):
+    """Arguments the reference refuses are refused here too, with -1 (or null) and no change to the
+    batch: a difficulty above 1 or NaN, a seed below -1 or above 2^32 - 1, a reverse flag other than
+    0 or 1, and an environment index outside the batch."""
+    import ctypes
+    import math
+
+    batches = _pair(host_library, '5_vs_5_l4_r0', 3, 4)
+    ref, mine = batches
+    p = ctypes.c_void_p
+    for b in batches:
+        b.lib.cuju_environment_set_difficulty.argtypes = [p, p]
+        b.lib.cuju_environment_get_state.argtypes = [p, ctypes.c_int, p, p]
+        b.lib.cuju_environment_get_state.restype = p
+    try:
+        assert mine.reset() == ref.reset()
+
+        def codes(call):
+            return [call(b) for b in batches]
+
+        for bad in (1.5, math.nan):
+            values = (ctypes.c_float * 6)(*([0.5] * 5 + [bad]))
+            assert codes(lambda b: b.lib.cuju_environment_set_difficulty(b.handle, values)) == [-1, -1]
+        ones = (ctypes.c_ubyte * 3)(1, 1, 1)
+        for seeds in ([-2, 0, 0], [0, 2**32, 0]):
+            arr = (ctypes.c_longlong * 3)(*seeds)
+            assert codes(lambda b: b.lib.cuju_environment_reset_masked(b.handle, ones, 0, arr, None, None, 1)) == [-1, -1]
+        reverse = (ctypes.c_int * 3)(0, 2, 1)
+        assert codes(lambda b: b.lib.cuju_environment_reset(b.handle, None, reverse, None)) == [-1, -1]
+        size, episode = ctypes.c_ulonglong(), (ctypes.c_int * 25)()
+        for index in (-1, 3):
+            assert codes(lambda b: b.lib.cuju_environment_get_state(b.handle, index, ctypes.byref(size), episode)) == \
+                [None, None]
+        acts = [2] * (3 * ref.agents)
+        assert mine.step(acts) == ref.step(acts)
+        for index in range(3):
+            assert mine.engine_state(index) == ref.engine_state(index)
+    finally:
+        for b in batches:
+            b.close()
