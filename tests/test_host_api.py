@@ -475,3 +475,35 @@ def test_argument_refusals_equal_the_reference(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+def test_state_moves_between_batches_of_mixed_bundles(host_library):
+    """A state taken from one environment of the reference batch and loaded into the environment
+    of the same bundle in both batches gives the same outputs and state from then on; loading it
+    into an environment of another bundle is refused by both."""
+    import ctypes
+
+    assets = ['academy_empty_goal_close_l1_r0', '5_vs_5_l4_r0']
+    batches = _pair(host_library, assets, 4, 8, assignment=[0, 1, 0, 1])
+    ref, mine = batches
+    rng = random.Random(41)
+    p = ctypes.c_void_p
+    try:
+        assert mine.reset() == ref.reset()
+        for step in range(25):
+            acts = [rng.randrange(19) for _ in range(4 * ref.agents)]
+            assert mine.step(acts) == ref.step(acts)
+        data, episode = ref.engine_state(3)
+        values = (ctypes.c_int * 25)(*episode[:25])
+        for b in batches:
+            b.lib.cuju_environment_set_state.argtypes = [p, ctypes.c_int, ctypes.c_char_p, ctypes.c_ulonglong, p]
+        assert [b.lib.cuju_environment_set_state(b.handle, 0, data, len(data), values) for b in batches] == [-1, -1]
+        assert mine.set_state(1, data, episode) == ref.set_state(1, data, episode)
+        for step in range(25):
+            acts = [rng.randrange(19) for _ in range(4 * ref.agents)]
+            assert mine.step(acts) == ref.step(acts), f'step {step} after the load differs'
+        for index in range(4):
+            assert mine.engine_state(index) == ref.engine_state(index)
+    finally:
+        for b in batches:
+            b.close()
