@@ -507,3 +507,25 @@ def test_state_moves_between_batches_of_mixed_bundles(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+@pytest.mark.parametrize('assets,representation,stack,checkpoints', [
+    ('11_vs_11_stochastic_l1_r1', 4, 4, True),
+    ('academy_3_vs_1_with_keeper_l3_r0', 8, 1, True),
+    ('5_vs_5_l4_r0', 1, 4, False),
+])
+def test_option_combinations(host_library, assets, representation, stack, checkpoints):
+    """Combinations the golden cases do not hold: stacked SMM with checkpoint rewards and a right
+    agent, raw with three agents and checkpoints, stacked simple115 (v1) with four agents."""
+    batches = _pair(host_library, assets, 3, 13, representation=representation, stack=stack,
+                    checkpoints=checkpoints)
+    ref, mine = batches
+    rng = random.Random(43)
+    try:
+        assert mine.reset() == ref.reset()
+        for step in range(50):
+            acts = [rng.randrange(19) for _ in range(3 * ref.agents)]
+            assert mine.step(acts) == ref.step(acts), f'step {step} differs'
+    finally:
+        for b in batches:
+            b.close()
