@@ -529,3 +529,25 @@ def test_option_combinations(host_library, assets, representation, stack, checkp
     finally:
         for b in batches:
             b.close()
+
+
+def test_first_index_at_the_end_of_the_seed_range(host_library):
+    """The last environments of the seed rule's 2^32 range play as the reference's, and a batch
+    that would run past the range is refused by both (reference tests/test_first_index.py)."""
+    from oracle.driver import OracleBatch
+
+    from conftest import ANIMATIONS, resolve
+
+    last = 2**32 - 3
+    batches = _pair(host_library, 'academy_empty_goal_close_l1_r0', 3, 6, first_index=last)
+    ref, mine = batches
+    try:
+        assert mine.reset() == ref.reset()
+        _run(batches, 60, random.Random(47))
+    finally:
+        for b in batches:
+            b.close()
+    paths, counts = resolve('academy_empty_goal_close_l1_r0')
+    for library in (None, host_library):
+        with pytest.raises(RuntimeError):
+            OracleBatch(paths, counts, 3, 6, ANIMATIONS, threads=1, library=library, first_index=last + 1)
