@@ -140,6 +140,7 @@ class BatchEnvironment:
         agent_counts: list[tuple[int | None, int | None]] | None = None,
         episode_number: int = 0,
         first_index: int = 0,
+        channel_dimensions: tuple[int, int] = (96, 72),
     ):
         if representation not in _REPRESENTATIONS:
             raise ChoiceError(f'expected one of {sorted(_REPRESENTATIONS)}, found {representation!r}')
@@ -183,7 +184,8 @@ class BatchEnvironment:
             animations=animations_path, environment_count=environment_count, seed=seed,
             action_set=_ACTION_SETS[action_set], observation=_REPRESENTATIONS[representation],
             checkpoints=int(self._checkpoints), numpy_legacy=int(numpy_legacy), auto_reset=int(auto_reset),
-            threads=0, ticks_per_step=physics_steps_per_frame, smm_width=96, smm_height=72,
+            threads=0, ticks_per_step=physics_steps_per_frame, smm_width=int(channel_dimensions[0]),
+            smm_height=int(channel_dimensions[1]),
             stack=4 if stacked else 1,
             fixed_seeds=ctypes.cast(fixed_array, ctypes.c_void_p) if fixed_array else None,
             agent_counts=ctypes.cast(counts_array, ctypes.c_void_p), episode_number=episode_number,
@@ -212,9 +214,12 @@ class BatchEnvironment:
         self._raw = representation == 'raw'
         self._smm = representation == 'extracted'
         if self._smm:
-            self._observation_shape = (environment_count, self.agents, 72, 96, 4 * stack)
+            # GRF's SMM is [height, width, channels] for `channel_dimensions` = (width, height).
+            self._observation_shape = (environment_count, self.agents, int(channel_dimensions[1]),
+                                       int(channel_dimensions[0]), 4 * stack)
         else:
             self._observation_shape = (environment_count, self.agents, 115 * stack)
+        self.channel_dimensions = (int(channel_dimensions[0]), int(channel_dimensions[1]))
         self._views = {}
 
     # -- plumbing ------------------------------------------------------------------------------

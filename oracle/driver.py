@@ -33,7 +33,7 @@ class OracleBatch:
     def __init__(self, bundle_paths, agent_counts, environment_count, seed, animations, threads=1,
                  representation=2, checkpoints=False, stack=1, assignment=None, difficulty=None,
                  auto_reset=True, ticks_per_step=10, first_index=0, library=None, fixed_seeds=None,
-                 episode_number=0, action_set=0, numpy_legacy=True):
+                 episode_number=0, action_set=0, numpy_legacy=True, smm_size=(96, 72)):
         path = library or LIBRARY
         if not os.path.isfile(path):
             raise RuntimeError(f'the oracle library is missing at {path}; run make -C oracle')
@@ -52,7 +52,7 @@ class OracleBatch:
             animations=animations.encode(), environment_count=environment_count, seed=seed,
             action_set=action_set, observation=representation, checkpoints=int(checkpoints),
             numpy_legacy=int(numpy_legacy),
-            auto_reset=int(auto_reset), threads=threads, ticks_per_step=ticks_per_step, smm_width=96, smm_height=72,
+            auto_reset=int(auto_reset), threads=threads, ticks_per_step=ticks_per_step, smm_width=smm_size[0], smm_height=smm_size[1],
             stack=stack, fixed_seeds=ctypes.cast(self._fixed, ctypes.c_void_p) if self._fixed else None,
             agent_counts=ctypes.cast(counts, ctypes.c_void_p), episode_number=episode_number, first_index=first_index, allocate=None, release=None, allocator_context=None,
             pin_threads=0, numa=0, page_aligned=0)
@@ -64,6 +64,7 @@ class OracleBatch:
         self.checkpoints = checkpoints
         self.width = 115 * stack
         self.representation = representation
+        self.smm_size = tuple(smm_size)
         if difficulty is not None:
             values = (ctypes.c_float * (2 * environment_count))(*difficulty)
             if self.lib.cuju_environment_set_difficulty(self.handle, values) != 0:
@@ -99,7 +100,7 @@ class OracleBatch:
         if self.representation == 8:
             obs = self._raw_bytes('raw')
         elif self.representation == 4:
-            obs = self._buffer('smm', e * a * 72 * 96 * 4 * (self.width // 115))
+            obs = self._buffer('smm', e * a * self.smm_size[0] * self.smm_size[1] * 4 * (self.width // 115))
         else:
             obs = self._buffer('simple115', 4 * e * a * self.width)
         return (obs, self._buffer('reward', 4 * e * a), self._buffer('done', e), self._buffer('score_reward', 4 * e))

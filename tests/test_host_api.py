@@ -551,3 +551,20 @@ def test_first_index_at_the_end_of_the_seed_range(host_library):
     for library in (None, host_library):
         with pytest.raises(RuntimeError):
             OracleBatch(paths, counts, 3, 6, ANIMATIONS, threads=1, library=library, first_index=last + 1)
+
+
+@pytest.mark.parametrize('size', [(48, 36), (120, 80)])
+def test_minimap_of_another_size(host_library, size):
+    """The SMM (`extracted`) minimap at a width and height other than GRF's default 96 x 72, stacked,
+    as the reference draws it (configuration smm_width / smm_height)."""
+    batches = _pair(host_library, '5_vs_5_l4_r0', 3, 17, representation=4, stack=4, smm_size=size)
+    ref, mine = batches
+    rng = random.Random(53)
+    try:
+        assert mine.reset() == ref.reset()
+        for step in range(40):
+            acts = [rng.randrange(19) for _ in range(3 * ref.agents)]
+            assert mine.step(acts) == ref.step(acts), f'step {step} differs'
+    finally:
+        for b in batches:
+            b.close()
