@@ -46,3 +46,30 @@ def test_calls_after_close_raise_closed_error():
         batch.get_state(0)
     with pytest.raises(ClosedError):
         batch.reset()
+
+
+def test_minimap_of_another_size_against_the_oracle():
+    """`channel_dimensions` = (48, 36): the SMM observation is [environments, agents, 36, 48, 4]
+    and equals the reference CPU backend's, byte for byte, over a reset and 20 steps."""
+    from conftest import ANIMATIONS, resolve
+
+    from cuju_b200 import BatchEnvironment
+    from oracle.driver import OracleBatch
+
+    paths, counts = resolve('5_vs_5_l4_r0')
+    mine = BatchEnvironment('5_vs_5_l4_r0', environment_count=3, seed=17, representation='extracted',
+                            channel_dimensions=(48, 36))
+    ref = OracleBatch(paths, counts, 3, 17, ANIMATIONS, threads=1, representation=4, smm_size=(48, 36))
+    try:
+        obs = mine.reset()
+        assert obs.shape == (3, 4, 36, 48, 4)
+        assert obs.cpu().numpy().tobytes() == ref.reset()[0]
+        for step in range(20):
+            actions = [[(step * 5 + e * 3 + a * 7) % 19 for a in range(4)] for e in range(3)]
+            got = mine.step(torch.tensor(actions, dtype=torch.int32).cuda())
+            want = ref.step([x for row in actions for x in row])
+            assert got[0].cpu().numpy().tobytes() == want[0], f'observation differs at step {step}'
+            assert got[1].cpu().numpy().tobytes() == want[1], f'reward differs at step {step}'
+    finally:
+        mine.close()
+        ref.close()
