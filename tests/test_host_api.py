@@ -568,3 +568,30 @@ def test_minimap_of_another_size(host_library, size):
     finally:
         for b in batches:
             b.close()
+
+
+@pytest.mark.parametrize('representation,stack', [(2, 1), (1, 4), (4, 1)])
+def test_final_observation_buffers_equal_the_reference(host_library, representation, stack):
+    """The observation that ended each episode (`final_simple115`, `final_smm`), which the automatic
+    restart keeps beside the new episode's first observation, equals the reference's after every
+    step of a drill that ends many episodes."""
+    batches = _pair(host_library, 'academy_empty_goal_close_l1_r0', 6, 59, representation=representation,
+                    stack=stack)
+    ref, mine = batches
+    name = 'final_smm' if representation == 4 else 'final_simple115'
+    per_env = (96 * 72 * 4 * stack) if representation == 4 else 4 * 115 * stack
+    rng = random.Random(61)
+    ended = 0
+    try:
+        assert mine.reset() == ref.reset()
+        for step in range(120):
+            acts = [rng.randrange(19) for _ in range(6 * ref.agents)]
+            out = ref.step(acts)
+            assert mine.step(acts) == out, f'step {step} differs'
+            ended += sum(out[2])
+            size = 6 * ref.agents * per_env
+            assert mine._buffer(name, size) == ref._buffer(name, size), f'{name} differs at step {step}'
+        assert ended > 0
+    finally:
+        for b in batches:
+            b.close()
