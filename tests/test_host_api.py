@@ -595,3 +595,24 @@ def test_final_observation_buffers_equal_the_reference(host_library, representat
     finally:
         for b in batches:
             b.close()
+
+
+def test_final_raw_equals_the_reference(host_library):
+    """`final_raw` (every raw array of each ended episode's last observation) equals the
+    reference's after every step of a drill that ends many episodes."""
+    batches = _pair(host_library, 'academy_empty_goal_close_l1_r0', 4, 67, representation=8)
+    ref, mine = batches
+    rng = random.Random(71)
+    try:
+        assert mine.reset() == ref.reset()
+        ended = 0
+        for step in range(100):
+            acts = [rng.randrange(19) for _ in range(4 * ref.agents)]
+            out = ref.step(acts)
+            assert mine.step(acts) == out, f'step {step} differs'
+            ended += sum(out[2])
+            assert mine._raw_bytes('final_raw') == ref._raw_bytes('final_raw'), f'final_raw differs at step {step}'
+        assert ended > 0
+    finally:
+        for b in batches:
+            b.close()
