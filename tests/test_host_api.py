@@ -616,3 +616,32 @@ def test_final_raw_equals_the_reference(host_library):
     finally:
         for b in batches:
             b.close()
+
+
+def test_a_difficulty_set_between_episodes_applies_from_the_next_reset(host_library):
+    """cuju_environment_set_difficulty during play changes nothing until an environment's next
+    reset, and then only the side it names (negative keeps the scenario's), as in the reference
+    (tests/test_difficulty.py)."""
+    import ctypes
+
+    batches = _pair(host_library, '11_vs_11_easy_stochastic_l1_r0', 3, 73)
+    ref, mine = batches
+    p = ctypes.c_void_p
+    for b in batches:
+        b.lib.cuju_environment_set_difficulty.argtypes = [p, p]
+    rng = random.Random(79)
+    try:
+        assert mine.reset() == ref.reset()
+        for step in range(30):
+            acts = [rng.randrange(19) for _ in range(3 * ref.agents)]
+            assert mine.step(acts) == ref.step(acts)
+            if step == 5:
+                values = (ctypes.c_float * 6)(0.9, -1.0, -1.0, 0.05, 0.5, 0.5)
+                assert [b.lib.cuju_environment_set_difficulty(b.handle, values) for b in batches] == [0, 0]
+            if step == 15:
+                assert mine.reset_masked([1, 0, 1], [5, -1, 7]) == ref.reset_masked([1, 0, 1], [5, -1, 7])
+        for index in range(3):
+            assert mine.engine_state(index) == ref.engine_state(index)
+    finally:
+        for b in batches:
+            b.close()
