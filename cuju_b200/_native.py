@@ -94,6 +94,9 @@ def declare(library: ctypes.CDLL) -> ctypes.CDLL:
     # This build's own extension; the reference libraries that the same declarations serve lack it.
     if hasattr(library, 'cuju_b200_environment_reset_masked_device'):
         library.cuju_b200_environment_reset_masked_device.argtypes = [p, p, p, p]
+    if hasattr(library, 'cuju_b200_environment_step_static'):
+        library.cuju_b200_environment_step_static.argtypes = [p, p, p]
+        library.cuju_b200_environment_step_static.restype = i
     library.cuju_environment_step.argtypes = [p, p, i, p, i]
     library.cuju_environment_step_async.argtypes = [p, p, i, p]
     library.cuju_environment_step_wait.argtypes = [p]

@@ -20,7 +20,8 @@ CSRC = os.path.join(HERE, 'csrc')
 LIB_DIR = os.path.join(HERE, 'lib')
 LIBRARY = os.path.join(LIB_DIR, 'libcuju_b200.so')
 DATA = os.path.join(HERE, 'data')
-REFERENCE = os.environ.get('CUJU_REFERENCE', '/root/reference')
+# The reference checkout: CUJU_REFERENCE, else a `reference` directory beside the repository.
+REFERENCE = os.environ.get('CUJU_REFERENCE') or os.path.normpath(os.path.join(ROOT, '..', 'reference'))
 
 NVCC_FLAGS = [
     '-std=c++17', '-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '-lineinfo',

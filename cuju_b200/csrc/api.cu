@@ -462,18 +462,20 @@ public:
         if (!actions) return "expected device actions";
         int device = -1;
         if (cudaGetDevice(&device) != cudaSuccess) return "no current CUDA device";
-        // A failed attribute query leaves a non-sticky error behind; it is cleared so that a later
-        // launch check does not report it.
+        // A failed attribute query leaves a non-sticky error behind. It is cleared so that a later
+        // launch check does not report it, but only when no error was pending before this call: an
+        // error the caller has not read yet stays for the caller.
+        const bool errorPending = cudaPeekAtLastError() != cudaSuccess;
         cudaPointerAttributes a{};
         if (cudaPointerGetAttributes(&a, actions) != cudaSuccess) {
-            (void)cudaGetLastError();
+            if (!errorPending) (void)cudaGetLastError();
             return "expected actions in device memory of the current device";
         }
         if ((a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) || a.device != device)
             return "expected actions in device memory of the current device";
         cudaPointerAttributes own{};
         if (cudaPointerGetAttributes(&own, b.status) != cudaSuccess) {
-            (void)cudaGetLastError();
+            if (!errorPending) (void)cudaGetLastError();
             return "expected the batch's device to be the current device";
         }
         if (own.device != device) return "expected the batch's device to be the current device";

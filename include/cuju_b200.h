@@ -98,7 +98,10 @@ int cuju_b200_kernel_info(unsigned long long *out);
  * nothing: no cudaMalloc/cudaFree, no host heap, no allocator callback. Asynchronous on `stream`
  * like cuju_environment_step_async; errors inside the step surface at the next
  * cuju_environment_synchronize. The first call on a device looks up the array's address with
- * cudaGetSymbolAddress while that device is current; make it before any stream capture. Nothing
+ * cudaGetSymbolAddress while that device is current; make it before any stream capture. The
+ * address is kept for the life of the process: after cudaDeviceReset (or anything else that
+ * replaces the device's primary context) the kept address is stale, so do not call this entry
+ * point again in that process. Nothing
  * in the array needs to start at zero (every sort writes what it reads). Calls that overlap in
  * time on one device (any stream, any batch) share the array and race: issue them one at a time.
  * Returns 0, or -1 with the reason in cuju_last_error (more than 32 environments, host or foreign

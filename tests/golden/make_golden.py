@@ -11,7 +11,9 @@ import json
 import os
 import sys
 
-REFERENCE = os.environ.get('CUJU_REFERENCE', '/root/reference')
+# The reference checkout: CUJU_REFERENCE, else a `reference` directory beside the repository.
+REFERENCE = os.environ.get('CUJU_REFERENCE') or os.path.normpath(
+    os.path.join(os.path.dirname(os.path.abspath(__file__)), '..', '..', '..', 'reference'))
 
 
 def main():
