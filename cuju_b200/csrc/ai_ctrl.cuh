@@ -308,9 +308,9 @@ struct AIController {
         auto time_at = [&](unsigned int qt) {
             if (qt < firstCached || qt >= firstCached + 10 * cached) {
                 firstCached = qt;
-                cached = in_region() ? 1 : 32;
+                cached = crew_serial() ? 1 : (unsigned int)crew_width();
                 uint64_t packed[32];
-                par_map<uint64_t>((int)cached,
+                crew_map<uint64_t>((int)cached,
                                   [&](int ln) {
                                       const unsigned int lt = qt + 10 * (unsigned int)ln;
                                       if (lt >= kPredictionSpan_ms) return (uint64_t)0;

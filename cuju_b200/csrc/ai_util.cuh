@@ -478,7 +478,7 @@ CB_HDNI void closest_players(PlayerList &r, const Sim &s, int teamID, const Vec3
         c.eligible = (!onlyAI || !external_active(w, p)) && (!onlySelectable || formation(s, p).controllable);
         return c;
     };
-    par_pipeline<Cand>(w.m.playerCount, eval, [&](int p, const Cand &c) {
+    crew_pipeline<Cand>(w.m.playerCount, eval, [&](int p, const Cand &c) {
         if (!c.eligible) return;
         const float d = c.distance;
         int slot = count++;

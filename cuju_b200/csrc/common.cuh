@@ -35,6 +35,30 @@
 namespace cb {
 
 // ---------------------------------------------------------------------------------------------
+// The per-thread crew byte (its layout and the crews themselves: crew.cuh). One bit of it marks
+// that the environment the thread works on reached an iteration cap of GRF's arithmetic.
+constexpr int kCrewSlots = 128;  // threads per block at most (the kernels launch 64)
+constexpr uint8_t kCrewWidthBits = 0x07;
+constexpr uint8_t kCrewDividedBit = 0x08;
+constexpr uint8_t kCrewCapBit = 0x10;
+#if CB_DEVICE_PASS
+__device__ __forceinline__ uint8_t &crew_byte() {
+    __shared__ uint8_t bytes[kCrewSlots];
+    return bytes[threadIdx.x];
+}
+CB_HD int lane_id() { return (int)(threadIdx.x & 31); }
+#else
+inline uint8_t &crew_byte() {
+    static thread_local uint8_t byte = 0;
+    return byte;
+}
+CB_HD int lane_id() { return 0; }
+#endif
+CB_HD void crew_note_cap() { crew_byte() |= kCrewCapBit; }
+CB_HD bool crew_cap_reached() { return (crew_byte() & kCrewCapBit) != 0; }
+CB_HD void crew_clear_cap() { crew_byte() &= (uint8_t)~kCrewCapBit; }
+
+// ---------------------------------------------------------------------------------------------
 // Bit casts
 CB_HD uint32_t f2u(float v) {
 #if CB_DEVICE_PASS
@@ -102,13 +126,16 @@ CB_HD int sign_side(float v) { return v >= 0 ? 1 : -1; }
 // that every caller passes, the loops end for |v| below 2^27 (above it v - span rounds back to v)
 // and take at most about 18.1 million iterations there; the cap of 2^25 per loop changes no
 // result where they end, and stops them where they would not (an infinite or huge angle, which
-// GRF leaves undefined) instead of holding the launch forever.
+// GRF leaves undefined) instead of holding the launch forever. Reaching the cap marks the
+// environment (crew_note_cap), so its step ends in the unsupported-path status.
 CB_HD float wrap_range(float lo, float hi, float v) {
     constexpr unsigned kCap = 1u << 25;
     float span = hi - lo;
     float r = v;
     for (unsigned i = 0; r < lo && i < kCap; i++) r += span;
+    if (r < lo) crew_note_cap();
     for (unsigned i = 0; r > hi && i < kCap; i++) r -= span;
+    if (r > hi) crew_note_cap();
     return r;
 }
 // A float written with printf("%f") and read back with atof, then narrowed to float: the exact

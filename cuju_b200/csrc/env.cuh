@@ -270,7 +270,7 @@ struct Observation {
 /// environment.h:387 (EnvironmentGetState).
 CB_HDNI void environment_get_state(Match &w, const Context &ctx, Observation &o) {
     const MatchState &m = w.m;
-    par_copy_words(reinterpret_cast<uint32_t *>(&o), nullptr, (int)(sizeof(Observation) / 4));
+    crew_copy_words(reinterpret_cast<uint32_t *>(&o), nullptr, (int)(sizeof(Observation) / 4));
     o.team[0].designatedPlayer = -1;
     o.team[1].designatedPlayer = -1;
     auto set3 = [](float *out, const Vec3 &v) {
@@ -639,7 +639,7 @@ CB_HD Sim make_sim(const Batch &b, int e, const Context &ctx) {
 CB_HDNI bool reset_environment(const Batch &b, int e, const int64_t *seeds, const int32_t *reverse) {
     EnvSlot &slot = b.slots[e];
     // Lane 0 keeps the books; the other lanes read them after the barrier.
-    wsync();
+    crew_sync();
     if (leader()) {
         const bool given = seeds && seeds[e] >= 0;
         const bool fixed = slot.fixedSeed >= 0;
@@ -655,27 +655,27 @@ CB_HDNI bool reset_environment(const Batch &b, int e, const int64_t *seeds, cons
         slot.variant = variant_of(slot);
         if (deterministic) slot.seed = b.variants[slot.variant].tmpl->scenario.gameEngineRandomSeed;
     }
-    wsync();
+    crew_sync();
     struct {
         int32_t variant;
         uint32_t seed;
     } sl = {slot.variant, slot.seed};
     const Variant &v = b.variants[sl.variant];
     Match &w = b.worlds[e];
-    par_copy(w, *v.tmpl);
+    crew_copy(w, *v.tmpl);
     // The difficulty goes in before the ticks that bring the match into play, which read it.
     if (b.teamDifficulty) {
         const float l = b.teamDifficulty[e * 2], r = b.teamDifficulty[e * 2 + 1];
         if (l >= 0.0f) w.scenario.leftTeamDifficulty = l;
         if (r >= 0.0f) w.scenario.rightTeamDifficulty = r;
     }
-    wsync();
+    crew_sync();
     Sim s = make_sim(b, e, v.ctx);
     if (!reset_from_template(s, sl.seed) || !core_after_reset(s, b.cores[e])) return false;
-    wsync();
+    crew_sync();
     for (int a = 0; a < kAgentsMax; a++) slot.collected[a] = 0;
     update_sticky(b, w, slot);
-    wsync();
+    crew_sync();
     return true;
 }
 
@@ -821,11 +821,19 @@ CB_HDNI void write_agent_outputs(const Batch &b, int e, int agent, bool afterSte
 
 // One agent per lane.
 CB_HDNI void write_env_outputs(const Batch &b, int e, bool afterStep) {
-    wsync();
+    crew_sync();
     const EnvSlot &slot = b.slots[e];
     const int n = slot.leftAgents + slot.rightAgents;
-    par_for(n, [&](int a) { write_agent_outputs(b, e, a, afterStep); });
-    wsync();
+    crew_for(n, [&](int a) { write_agent_outputs(b, e, a, afterStep); });
+    crew_sync();
+}
+
+// An iteration cap of GRF's arithmetic reached during a call (crew_note_cap) marks a path GRF
+// leaves undefined: the environment's status says so, and the host raises it at the next
+// synchronising call.
+CB_HD void settle_caps(const Batch &b, int e) {
+    if (crew_cap_reached() && b.status[e] == kStatusOk) b.status[e] = kStatusUnsupported;
+    crew_clear_cap();
 }
 
 CB_HDNI bool reset_and_write(const Batch &b, int e, const int64_t *seeds, const int32_t *reverse) {
@@ -842,7 +850,7 @@ CB_HDNI bool step_environment(const Batch &b, int e, const int32_t *actions) {
     EnvSlot &slot = b.slots[e];
     const int agents = slot.leftAgents + slot.rightAgents;
     if (!b.autoReset && b.done[e]) {
-        wsync();
+        crew_sync();
         if (leader()) {
             for (int a = 0; a < b.agents; a++) b.reward[(size_t)e * b.agents + a] = 0.0f;
             b.scoreReward[e] = 0;
@@ -864,9 +872,9 @@ CB_HDNI bool step_environment(const Batch &b, int e, const int32_t *actions) {
     Match &w = b.worlds[e];
     Sim s = make_sim(b, e, b.variants[slot.variant].ctx);
     if (!core_step(s, b.cores[e], ea, reward, done)) return false;
-    wsync();
+    crew_sync();
     update_sticky(b, w, slot);
-    wsync();
+    crew_sync();
     if (leader()) {
         for (int a = 0; a < b.agents; a++)
             b.reward[(size_t)e * b.agents + a] = a < agents ? (float)(a < slot.leftAgents ? reward : -reward) : 0.0f;
@@ -876,7 +884,7 @@ CB_HDNI bool step_environment(const Batch &b, int e, const int32_t *actions) {
     write_env_outputs(b, e, true);
     if (done && leader())
         for (int t = 0; t < 2; t++) slot.finalDesignated[t] = b.cores[e].observation.team[t].designatedPlayer;
-    wsync();
+    crew_sync();
     if (!b.autoReset || !done) return true;
     if (!reset_environment(b, e, nullptr, nullptr)) return false;
     write_env_outputs(b, e, false);

@@ -555,7 +555,7 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
         }
         if (mayRequeue) h.interruptAnim = kIntReQueue;
     }
-    if (!warp_assisted(s, p, h.interruptAnim != kIntNone,
+    if (!crew_assist(s, p, h.interruptAnim != kIntNone,
                        [](const Sim &sim, int player) { return humanoid_interrupt(sim, player); }))
         return false;
     h.requeueDelayFrames = h.requeueDelayFrames - 1 > 0 ? h.requeueDelayFrames - 1 : 0;
@@ -576,7 +576,7 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
     bool ctrlColl = pl.triggerControlledBallCollision;
     if (ctrlColl) pl.triggerControlledBallCollision = false;
     const bool touches = (ctrlColl && ca.touchFrame == -1) || ca.touchFrame == ca.frameNumber || w.m.ballRetainer == p;
-    if (!warp_assisted(s, p | (ctrlColl ? 0x10000 : 0), touches,
+    if (!crew_assist(s, p | (ctrlColl ? 0x10000 : 0), touches,
                        [](const Sim &sim, int touchArg) { return humanoid_touches(sim, touchArg); }))
         return false;
     const int eff = a.frameCount - 1;

@@ -1,7 +1,7 @@
-// cuju-b200: the batch kernels. One lane per environment: each thread runs its environment's
-// whole step (every warp-cooperative construct of warp.cuh runs serially on the lane), so a warp
-// advances 32 environments at once and a batch of 16,384 is resident in one wave. The host
-// launches them through the wrappers at the end, on the caller's stream.
+// cuju-b200: the batch kernels. Every lane starts as a crew of one that owns an environment and
+// runs its whole step (crew.cuh); branches with wide loops are dealt to larger crews of the same
+// warp (crew_assist). A warp advances 32 environments at once and a batch of 16,384 is resident in
+// one wave. The host launches the kernels through the wrappers at the end, on the caller's stream.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -17,10 +17,11 @@ __device__ __forceinline__ void report(const Batch &b, int e) {
 __device__ __forceinline__ int env_index() { return (int)(blockIdx.x * blockDim.x + threadIdx.x); }
 
 __global__ void __launch_bounds__(kThreadsPerBlock) step_kernel(Batch b, const int32_t *__restrict__ actions) {
-    lane_mode_begin();
+    crew_start();
     const int e = env_index();
     if (e >= b.count || b.status[e] != kStatusOk) return;
     step_environment(b, e, actions);
+    settle_caps(b, e);
     report(b, e);
 }
 
@@ -28,16 +29,17 @@ __global__ void __launch_bounds__(kThreadsPerBlock) step_kernel(Batch b, const i
 __global__ void __launch_bounds__(kThreadsPerBlock) reset_kernel(Batch b, const uint8_t *__restrict__ mask,
                                                                  const int64_t *__restrict__ seeds,
                                                                  const int32_t *__restrict__ reverse) {
-    lane_mode_begin();
+    crew_start();
     const int e = env_index();
     if (e >= b.count || (mask && !mask[e]) || b.status[e] != kStatusOk) return;
     reset_and_write(b, e, seeds, reverse);
+    settle_caps(b, e);
     report(b, e);
 }
 
 // Rewrites the outputs of the masked environments from their observations (after a state load).
 __global__ void __launch_bounds__(kThreadsPerBlock) output_kernel(Batch b, const uint8_t *__restrict__ mask) {
-    lane_mode_begin();
+    crew_start();
     const int e = env_index();
     if (e >= b.count || (mask && !mask[e])) return;
     write_env_outputs(b, e, false);

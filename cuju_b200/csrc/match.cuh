@@ -128,11 +128,11 @@ CB_HDNI void push_mental_image(Match &w) {
     MatchState &m = w.m;
     const int n = m.mentalImages.count < 3 ? m.mentalImages.count + 1 : 3;
     for (int i = n - 1; i > 0; i--) {
-        par_copy(m.mentalImages.el[i], m.mentalImages.el[i - 1]);
+        crew_copy(m.mentalImages.el[i], m.mentalImages.el[i - 1]);
         w.flags.mentalBallMirrored[i] = w.flags.mentalBallMirrored[i - 1];
     }
     MentalImage &im = m.mentalImages.el[0];
-    par_copy_words(reinterpret_cast<uint32_t *>(&im), nullptr, (int)(sizeof(MentalImage) / 4));
+    crew_copy_words(reinterpret_cast<uint32_t *>(&im), nullptr, (int)(sizeof(MentalImage) / 4));
     im.timeStamp_ms = (uint32_t)m.actualTime_ms;
     im.maxDistanceDeviation = 2.5f;
     im.maxMovementDeviation = kWalkVel;
@@ -156,7 +156,7 @@ CB_HDNI void push_mental_image(Match &w) {
     }
     const int np = (int)(kPredictionSpan_ms / 10);
     im.ballPredictions.count = np;
-    par_copy_words(reinterpret_cast<uint32_t *>(im.ballPredictions.el),
+    crew_copy_words(reinterpret_cast<uint32_t *>(im.ballPredictions.el),
                    reinterpret_cast<const uint32_t *>(m.ball.predictions), np * 3);
     im.lazyFlip = m.ball.lazyFlip;
     w.flags.mentalBallMirrored[0] = false;
@@ -389,13 +389,13 @@ CB_HDNI void match_prepare_put_buffers(const Sim &s) {
     {
         PlayerList ps;
         active_players(ps, w, first);
-        par_for(ps.count, [&](int i) { player_prepare_put_buffers(s, ps[i]); });
+        crew_for(ps.count, [&](int i) { player_prepare_put_buffers(s, ps[i]); });
     }
     mirror_match(w, false, false, true);
     {
         PlayerList ps;
         active_players(ps, w, second);
-        par_for(ps.count, [&](int i) { player_prepare_put_buffers(s, ps[i]); });
+        crew_for(ps.count, [&](int i) { player_prepare_put_buffers(s, ps[i]); });
     }
     mirror_match(w, false, false, first == 0);
 }
@@ -424,8 +424,8 @@ CB_HDNI bool match_fetch_put_buffers(const Sim &s) {
         if (!apply_prepare(T, a, h, b.smooth, b.frameNumber, plans[i])) return s.fail(kStatusOverflow);
         firstNode[i + 1] = firstNode[i] + a.nodeCount;
     }
-    wsync();
-    par_for(firstNode[n], [&](int item) {
+    crew_sync();
+    crew_for(firstNode[n], [&](int item) {
         int hi = 0;
         while (firstNode[hi + 1] <= item) hi++;
         Humanoid &h = any_hum(w, hidx[hi]);

@@ -9,7 +9,7 @@
 
 #include "ball.cuh"
 #include "tables.cuh"
-#include "warp.cuh"
+#include "crew.cuh"
 
 namespace cb {
 
@@ -88,42 +88,70 @@ struct Sim {
     }
 };
 
-// Runs fn(sim, arg) for the environment of every lane whose `need` is set and returns that lane's
-// result (true where not needed). In lane mode, when all 32 lanes of the warp execute this call
-// together, the calls are taken one environment at a time by the whole warp in warp mode, so the
-// wide loops inside them (animation filters, candidate sorts) split across 32 lanes instead of
-// running on one lane while the others wait; otherwise every lane makes its own call. `fn` must
-// read and write only device memory reachable from the Sim, never the calling lane's locals.
-#if CB_DEVICE_PASS
-__device__ __forceinline__ unsigned long long shfl_word(unsigned long long v, int src) {
-    return __shfl_sync(0xffffffffu, v, src);
-}
-#endif
+// Runs fn(sim, arg) for the environment of every lane whose `need` is set, and returns the calling
+// lane's result (true where not needed). When the 32 lanes of a warp of crews of one reach the call
+// together, the k environments that need it are dealt to crews: c crews of 32/c lanes, c the
+// smallest power of two at least k (at most kAssistCrewsMax), in rounds of c environments. Each
+// crew runs fn for its environment and divides the wide loops inside (animation filters, candidate
+// sorts, ball prediction scans) between its lanes, instead of one lane running them while the
+// others wait. Otherwise every lane makes its own call. `fn` must read and write only device memory
+// reachable from the Sim it is given, never the calling lane's locals. The result and any
+// iteration-cap mark of an environment go back to the lane that owns it.
+constexpr int kAssistCrewsMax = 4;
+
 template <class Fn>
-CB_HD bool warp_assisted(const Sim &s, int arg, bool need, Fn fn) {
+CB_HD bool crew_assist(const Sim &s, int arg, bool need, Fn fn) {
 #if CB_DEVICE_PASS
-    if (lane_env() && __activemask() == 0xffffffffu) {
-        unsigned pending = __ballot_sync(0xffffffffu, need);
-        bool mine = true;
-        while (pending) {
-            const int src = __ffs(pending) - 1;
-            pending &= pending - 1;
-            Match *w = reinterpret_cast<Match *>(shfl_word(reinterpret_cast<unsigned long long>(&s.w), src));
-            const Context *c =
-                reinterpret_cast<const Context *>(shfl_word(reinterpret_cast<unsigned long long>(&s.ctx), src));
-            WarpScratch *sc = reinterpret_cast<WarpScratch *>(shfl_word(reinterpret_cast<unsigned long long>(s.scratch), src));
-            int32_t *st = reinterpret_cast<int32_t *>(shfl_word(reinterpret_cast<unsigned long long>(s.status), src));
-            const int a = __shfl_sync(0xffffffffu, arg, src);
-            const Sim shared{*w, *c, sc, st};
-            __syncwarp();
-            if (lane_id() == 0) region_flag() = 0;
-            __syncwarp();
-            const bool r = fn(shared, a);
-            __syncwarp();
-            if (lane_id() == 0) region_flag() = 2;
-            __syncwarp();
-            if (lane_id() == src) mine = r;
+    if (crew_owns_env() && __activemask() == 0xffffffffu) {
+        const unsigned full = 0xffffffffu;
+        const unsigned pending = __ballot_sync(full, need);
+        if (!pending) return true;
+        const int k = __popc(pending);
+        int log2c = 0;
+        while ((1 << log2c) < k && (1 << log2c) < kAssistCrewsMax) log2c++;
+        const int crews = 1 << log2c, log2w = 5 - log2c, width = 1 << log2w;
+        const unsigned widthBits = width == 32 ? full : (1u << width) - 1u;
+        const int lane = lane_id();
+        const int crew = lane >> log2w;
+        const int myPlace = __popc(pending & ((1u << lane) - 1u));
+        const bool ownCap = crew_cap_reached();
+        bool mine = true, myCap = false;
+        for (int first = 0; first < k; first += crews) {
+            // The environment this lane's crew runs in this round: the (first + crew)-th that needs it.
+            const int place = first + crew;
+            unsigned rest = pending;
+            for (int i = 0; i < place && rest; i++) rest &= rest - 1;
+            const int src = place < k ? __ffs(rest) - 1 : lane;
+            Match *wp = reinterpret_cast<Match *>(
+                __shfl_sync(full, reinterpret_cast<unsigned long long>(&s.w), src));
+            const Context *cp = reinterpret_cast<const Context *>(
+                __shfl_sync(full, reinterpret_cast<unsigned long long>(&s.ctx), src));
+            WarpScratch *sp = reinterpret_cast<WarpScratch *>(
+                __shfl_sync(full, reinterpret_cast<unsigned long long>(s.scratch), src));
+            int32_t *stp = reinterpret_cast<int32_t *>(
+                __shfl_sync(full, reinterpret_cast<unsigned long long>(s.status), src));
+            const int a = __shfl_sync(full, arg, src);
+            __syncwarp(full);
+            crew_clear_cap();
+            bool r = true;
+            if (place < k) {
+                crew_set(log2w);
+                const Sim shared{*wp, *cp, sp, stp};
+                r = fn(shared, a);
+                crew_set(0);
+            }
+            __syncwarp(full);
+            const unsigned caps = __ballot_sync(full, crew_cap_reached());
+            const bool served = need && myPlace >= first && myPlace < first + crews;
+            const int from = served ? (myPlace - first) << log2w : lane;
+            const int got = __shfl_sync(full, (int)r, from);
+            if (served) {
+                mine = got != 0;
+                myCap = ((caps >> from) & widthBits) != 0;
+            }
         }
+        crew_clear_cap();
+        if (ownCap || myCap) crew_note_cap();
         return mine;
     }
 #endif
@@ -198,7 +226,7 @@ CB_HDNI void mirror_humanoid(Humanoid &h, bool &mirrored) {
 CB_HD void mirror_team(Match &w, int teamID) {
     w.flags.teamSide[teamID] *= -1;
     w.flags.teamMirrored[teamID] = !w.flags.teamMirrored[teamID];
-    par_for(w.m.playerCount, [&](int p) {
+    crew_for(w.m.playerCount, [&](int p) {
         if (w.playerTeamID[p] == teamID) mirror_humanoid(w.m.players[p].base.humanoid, w.flags.humanoidMirrored[p]);
     });
 }
@@ -211,7 +239,7 @@ CB_HD void mirror_ball(Ball &b) {
 CB_HD void ball_materialize(Ball &b) {
     if (!b.lazyFlip) return;
     const int n = 401;
-    par_for(n + b.positionHistory.count, [&](int i) {
+    crew_for(n + b.positionHistory.count, [&](int i) {
         if (i < n) b.predictions[i].mirror();
         else b.positionHistory[i - n].mirror();
     });
@@ -219,12 +247,12 @@ CB_HD void ball_materialize(Ball &b) {
 }
 CB_HD void mental_materialize(MentalImage &im) {
     if (!im.lazyFlip) return;
-    par_for(im.ballPredictions.count, [&](int i) { im.ballPredictions[i].mirror(); });
+    crew_for(im.ballPredictions.count, [&](int i) { im.ballPredictions[i].mirror(); });
     im.lazyFlip = false;
 }
 CB_HD void mirror_mental(Match &w, int idx, bool t0, bool t1, bool ball) {
     MentalImage &im = w.m.mentalImages[idx];
-    par_for(im.players.count, [&](int i) {
+    crew_for(im.players.count, [&](int i) {
         PlayerImage &pi = im.players[i];
         int team = w.playerTeamID[pi.player];
         if (team == 0 ? t0 : t1) {

@@ -62,7 +62,7 @@ CB_HDNI Vec3 force_field_movement(const ForceField &f, const Vec3 &pos, float da
         }
         return t;
     };
-    par_pipeline<Term>(f.count, term, [&](int, const Term &t) {
+    crew_pipeline<Term>(f.count, term, [&](int, const Term &t) {
         if (t.active) {
             cv += t.contribution;
             cf += t.force;
@@ -101,7 +101,7 @@ CB_HDNI void mental_team_images(const Match &w, int mi, int teamID, ImageList &o
         e.valid = 1;
         return e;
     };
-    par_pipeline<Entry>(im.players.count, img, [&](int, const Entry &e) {
+    crew_pipeline<Entry>(im.players.count, img, [&](int, const Entry &e) {
         if (e.valid) out.push(ImagePos{e.position, e.movement, e.role});
     });
 }
@@ -308,7 +308,7 @@ CB_HDNI bool official_process(const Sim &s, int official) {
     ca.frameNumber++;
     h.prevAnimFrameNumber++;
     if (ca.frameNumber == s.A(ca.anim).frameCount - 1 && h.interruptAnim == kIntNone) h.interruptAnim = kIntSwitch;
-    if (!warp_assisted(s, official, h.interruptAnim != kIntNone,
+    if (!crew_assist(s, official, h.interruptAnim != kIntNone,
                        [](const Sim &sim, int o) { return official_interrupt(sim, o); }))
         return false;
     h.requeueDelayFrames = (int)clampf_((float)(h.requeueDelayFrames - 1), 0, 10000);

@@ -55,7 +55,7 @@ CB_HDNI bool humanoid_reset_position(const Sim &s, int h, const Vec3 &np, const 
     ca.id = idle;
     ca.anim = idle;
     ca.positions.count = a.positionCount;
-    par_copy_words(reinterpret_cast<uint32_t *>(ca.positions.el),
+    crew_copy_words(reinterpret_cast<uint32_t *>(ca.positions.el),
                    reinterpret_cast<const uint32_t *>(s.T().positions + a.firstPosition), 3 * a.positionCount);
     // The frame draws below the effective frame count, one less than the frame count.
     ca.frameNumber = cvt_f_i32(random_in_range(w.rng, 0, (float)(a.frameCount - 1 - 1)));
@@ -232,7 +232,7 @@ CB_HDNI void ball_reset_situation(Ball &b, const Vec3 &focus) {
     b.momentum = Vec3(0);
     b.rotationPerMs = Quat();
     const Vec3 p = focus + Vec3(0, 0, 0.11f);
-    par_for(kPredictionSpan_ms / 10, [&](int i) { b.predictions[i] = p; });
+    crew_for(kPredictionSpan_ms / 10, [&](int i) { b.predictions[i] = p; });
     b.orientationPrediction = Quat();
     b.positionHistory.count = 0;
     b.positionBuffer = p;

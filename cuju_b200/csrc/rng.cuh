@@ -69,7 +69,8 @@ struct MatchRng {
     // Boost uniform_real<float>: Next()/2^32 in float, redrawn when it rounds up to the maximum.
     // A redraw happens about once in 2^25 draws for a range of [0, 1), so no match redraws 2^16
     // times in a row; the cap only ends the loop for a stored range where no draw can fall below
-    // the maximum (equal or NaN bounds in corrupted state), which would otherwise never return.
+    // the maximum (equal or NaN bounds in corrupted state), which would otherwise never return; it
+    // marks the environment (crew_note_cap), so the step ends in the unsupported-path status.
     CB_HD float uniform() {
         const float mn = lo(), mx = hi();
         float r = mn;
@@ -79,6 +80,7 @@ struct MatchRng {
             r = num / div * (mx - mn) + mn;
             if (r < mx) return r;
         }
+        crew_note_cap();
         return r;
     }
 };

@@ -150,21 +150,24 @@ CB_HDNI void stable_sort(const Sim &s, AnimList &list, KeyFn key) {
     const int n = list.count;
     if (n < 2) return;
 #if CB_DEVICE_PASS
-    if (!in_region()) {
+    if (!crew_serial()) {
+        // A crew sorts (key, position) pairs in the environment's scratch with a bitonic network.
         WarpScratch &sc = *s.scratch;
         int N = 1;
         while (N < n) N <<= 1;
-        const int lane = lane_id();
-        __syncwarp();
-        region_enter();
-        for (int i = lane; i < N; i += 32) {
-            sc.keys[i] = i < n ? (double)key((int)list[i]) : (double)INFINITY;
-            sc.idx[i] = (int16_t)(i < n ? i : 32767);
+        const int rank = crew_rank(), w = crew_width();
+        crew_sync();
+        {
+            CrewDivided divided;
+            for (int i = rank; i < N; i += w) {
+                sc.keys[i] = i < n ? (double)key((int)list[i]) : (double)INFINITY;
+                sc.idx[i] = (int16_t)(i < n ? i : 32767);
+            }
         }
-        region_leave();
+        crew_sync();
         for (int k = 2; k <= N; k <<= 1) {
             for (int j = k >> 1; j > 0; j >>= 1) {
-                for (int t = lane; t < N / 2; t += 32) {
+                for (int t = rank; t < N / 2; t += w) {
                     // t-th pair of this stage: lower element i with bit j clear.
                     int i = ((t / j) * 2 * j) + (t % j);
                     int l = i + j;
@@ -177,17 +180,17 @@ CB_HDNI void stable_sort(const Sim &s, AnimList &list, KeyFn key) {
                         sc.idx[i] = (int16_t)il; sc.idx[l] = (int16_t)ii;
                     }
                 }
-                __syncwarp();
+                crew_sync();
             }
         }
-        for (int i = lane; i < n; i += 32) sc.list[i] = list[sc.idx[i]];
-        __syncwarp();
+        for (int i = rank; i < n; i += w) sc.list[i] = list[sc.idx[i]];
+        crew_sync();
         for (int i = 0; i < n; i++) list[i] = sc.list[i];
-        __syncwarp();
+        crew_sync();
         return;
     }
 #endif
-    if (lane_env() && s.scratch) {
+    if (crew_owns_env() && s.scratch) {
         // The lane owns the environment's scratch: each key once, then a bottom-up stable merge
         // sort of (key, position) runs, the left run winning ties.
         WarpScratch &sc = *s.scratch;
@@ -257,36 +260,39 @@ template <class KeysFn>
 CB_HDNI int first_of_chain(const AnimList &list, int nkeys, KeysFn keys) {
     const int n = list.count;
     if (n < 2) return list[0];
-    bool nested;
-    int lane, stride;
-    split(nested, lane, stride);
-#if CB_DEVICE_PASS
-    if (!nested) region_enter();
-#endif
+    const bool serial = crew_serial();
+    const int rank = serial ? 0 : crew_rank(), w = serial ? 1 : crew_width();
     int best = -1;
     double bk[kMaxChainKeys];
-    for (int e = lane; e < n; e += stride) {
-        double ek[kMaxChainKeys];
-        keys((int)list[e], ek);
-        if (best < 0 || chain_precedes(ek, bk, nkeys)) {
-            best = e;
-            for (int k = 0; k < nkeys; k++) bk[k] = ek[k];
+    {
+#if CB_DEVICE_PASS
+        crew_sync();
+        CrewDivided divided(!serial);
+#endif
+        for (int e = rank; e < n; e += w) {
+            double ek[kMaxChainKeys];
+            keys((int)list[e], ek);
+            if (best < 0 || chain_precedes(ek, bk, nkeys)) {
+                best = e;
+                for (int k = 0; k < nkeys; k++) bk[k] = ek[k];
+            }
         }
     }
 #if CB_DEVICE_PASS
-    if (!nested) {
-        region_leave();
-        for (int off = 16; off > 0; off >>= 1) {
-            const int ob = __shfl_xor_sync(0xffffffffu, best, off);
+    if (!serial) {
+        // Each lane holds the best of its share; a butterfly over the crew keeps the smallest keys,
+        // the earliest position on a full tie, and every lane ends with the same answer.
+        const unsigned mask = crew_mask();
+        for (int off = w >> 1; off > 0; off >>= 1) {
+            const int ob = __shfl_xor_sync(mask, best, off, w);
             double ok[kMaxChainKeys];
-            for (int k = 0; k < nkeys; k++) ok[k] = __shfl_xor_sync(0xffffffffu, bk[k], off);
+            for (int k = 0; k < nkeys; k++) ok[k] = __shfl_xor_sync(mask, bk[k], off, w);
             if (ob >= 0 && (best < 0 || chain_precedes(ok, bk, nkeys) ||
                             (!chain_precedes(bk, ok, nkeys) && ob < best))) {
                 best = ob;
                 for (int k = 0; k < nkeys; k++) bk[k] = ok[k];
             }
         }
-        best = __shfl_sync(0xffffffffu, best, 0);
     }
 #endif
     return list[best];
@@ -501,7 +507,7 @@ CB_HDNI void crude_selection(const Sim &s, const CrudeQuery &q, AnimList &out) {
         return true;
     };
     int count = 0;
-    par_filter(0, cand, [&](int c) { return pass(lst ? lst[c] : c); },
+    crew_filter(0, cand, [&](int c) { return pass(lst ? lst[c] : c); },
                [&](int c) { out[count++] = (int16_t)(lst ? lst[c] : c); });
     out.count = count;
 }
@@ -728,7 +734,7 @@ struct Selector {
             bestQ = A(l[0]).quadrantID;
         }
         int kept = 1;
-        par_filter(1, l.count,
+        crew_filter(1, l.count,
                    [&](int c) {
                        const Anim &a = A(l[c]);
                        if (strict) return a.quadrantID == bestQ;
@@ -753,7 +759,7 @@ struct Selector {
         if (strict && cmd.desiredFunctionType != kFtMovement) sort_base(l);
         float bestLook = look_angle(l[0]);
         int kept = 1;
-        par_filter(1, l.count,
+        crew_filter(1, l.count,
                    [&](int c) {
                        float la = look_angle(l[c]);
                        float aa = 0.06f * kPi;
@@ -942,7 +948,7 @@ struct Selector {
             f.curvedTime = physics_curved_time(frame);
             return f;
         };
-        par_pipeline<PhysicsFrame>(a.frameCount, pre, [&](int frame, const PhysicsFrame &f) {
+        crew_pipeline<PhysicsFrame>(a.frameCount, pre, [&](int frame, const PhysicsFrame &f) {
             const int tms = frame * dt;
             float fb = (tms + 10) / (float)((effFrames + 1) * 10);
             const Vec3 &am = f.animMovement;

@@ -326,7 +326,7 @@ CB_HDNI bool team_dynamic_roles(const Sim &s, int teamID) {
     for (int i = 0; i < n; i++) slots[i] = team_adapted_formation_position(s, players[i], false);
     // The integer distance of every (player, slot) pair, computed once.
     int icost[kTeamPlayers * kTeamPlayers];
-    par_map<int>(
+    crew_map<int>(
         n * n,
         [&](int k) {
             const int pi = k / n, si = k % n;
@@ -418,7 +418,7 @@ CB_HDNI void team_man_marking(const Sim &s, int teamID) {
         float bestQ = -1.0f;
         const int oppP = ai.opponentInfo.el[rank].player;
         float q[kTeamPlayers];
-        par_map<float>(
+        crew_map<float>(
             players.count,
             [&](int i) {
                 return formation(s, players[i]).role == kRoleGK ? -2.0f : marking_quality(w, teamID, players[i], oppP);

@@ -30,15 +30,19 @@ CB_HDNI void ball_process(Ball &b, bool inGoal) {
     } else {
         const int n = hist.count;
 #if CB_DEVICE_PASS
-        if (!in_region()) {
-            // Lanes shift disjoint entries: each reads before the barrier and writes after it.
-            Vec3 tmp[(kBallHistory + 31) / 32];
-            int slot = 0;
-            for (int e = lane_id() + 1; e < n; e += 32) tmp[slot++] = hist[e];
-            __syncwarp();
-            slot = 0;
-            for (int e = lane_id() + 1; e < n; e += 32) hist[e - 1] = tmp[slot++];
-            __syncwarp();
+        if (!crew_serial()) {
+            // A crew moves one block of entries per pass, one entry per lane: every lane reads its
+            // entry before the barrier and writes it one place down after it. A pass writes only
+            // below the entries later passes read.
+            const int w = crew_width();
+            for (int base = 1; base < n; base += w) {
+                const int e = base + crew_rank();
+                Vec3 v;
+                if (e < n) v = hist[e];
+                crew_sync();
+                if (e < n) hist[e - 1] = v;
+                crew_sync();
+            }
         } else
 #endif
         {
@@ -50,7 +54,7 @@ CB_HDNI void ball_process(Ball &b, bool inGoal) {
 
 CB_HDNI void team_possession_stats(const Sim &s, int teamID) {
     Match &w = s.w;
-    par_for(w.m.playerCount, [&](int p) {
+    crew_for(w.m.playerCount, [&](int p) {
         if (w.playerTeamID[p] == teamID && w.m.players[p].base.isActive)
             update_possession_stats(w, *s.ctx.staticData, p);
     });

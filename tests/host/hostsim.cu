@@ -36,7 +36,9 @@ namespace cb {
 cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t) {
     for (int e = 0; e < b.count; e++) {
         if (b.status[e]) continue;
+        crew_start();
         step_environment(b, e, actions);
+        settle_caps(b, e);
         if (b.status[e] && !*b.anyFail) { *b.anyFail = b.status[e]; fprintf(stderr, "env %d failed %d\n", e, b.status[e]); }
     }
     return cudaSuccess;
@@ -45,7 +47,9 @@ cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *see
     for (int e = 0; e < b.count; e++) {
         if (mask && !mask[e]) continue;
         if (b.status[e]) continue;
+        crew_start();
         reset_and_write(b, e, seeds, reverse);
+        settle_caps(b, e);
         if (b.status[e] && !*b.anyFail) { *b.anyFail = b.status[e]; fprintf(stderr, "env %d failed %d\n", e, b.status[e]); }
     }
     return cudaSuccess;
