@@ -555,6 +555,7 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
         }
         if (mayRequeue) h.interruptAnim = kIntReQueue;
     }
+    convoy_waypoint(2 + team_slot(w, teamID) * 64 + p * 2);
     if (!crew_assist(s, p, h.interruptAnim != kIntNone,
                        [](const Sim &sim, int player) { return humanoid_interrupt(sim, player); }))
         return false;

@@ -10,31 +10,49 @@
 
 namespace cb {
 
+static_assert(kConvoyWarps * 32 <= kCrewSlots, "a block's threads each need a crew byte and a convoy key");
+
 // A failed environment stops; the first failure code of the batch goes to `anyFail`.
 __device__ __forceinline__ void report(const Batch &b, int e) {
     if (b.status[e] != kStatusOk) atomicCAS(b.anyFail, 0, b.status[e]);
 }
 __device__ __forceinline__ int env_index() { return (int)(blockIdx.x * blockDim.x + threadIdx.x); }
+// The batch's warps spread evenly over the blocks (the first blocks take one warp more): warp w of
+// block k runs environments 32 * (k * base + min(k, extra) + w) onwards. A warp past its block's
+// share has none (count).
+__device__ __forceinline__ int env_index_spread(int count) {
+    const int warps = (count + 31) / 32, blocks = (int)gridDim.x, k = (int)blockIdx.x;
+    const int base = warps / blocks, extra = warps % blocks;
+    const int w = (int)(threadIdx.x >> 5);
+    if (w >= base + (k < extra ? 1 : 0)) return count;
+    return (k * base + (k < extra ? k : extra) + w) * 32 + lane_id();
+}
 
-__global__ void __launch_bounds__(kThreadsPerBlock) step_kernel(Batch b, const int32_t *__restrict__ actions) {
+__global__ void __launch_bounds__(kConvoyWarps * 32) step_kernel(Batch b, const int32_t *__restrict__ actions) {
     crew_start();
-    const int e = env_index();
-    if (e >= b.count || b.status[e] != kStatusOk) return;
+    const int e = env_index_spread(b.count);
+    const bool live = e < b.count && b.status[e] == kStatusOk;
+    convoy_start(live);
+    if (!live) return;
     step_environment(b, e, actions);
     settle_caps(b, e);
     report(b, e);
+    convoy_leave();
 }
 
 // Resets every environment whose mask entry is set (all for a null mask).
-__global__ void __launch_bounds__(kThreadsPerBlock) reset_kernel(Batch b, const uint8_t *__restrict__ mask,
-                                                                 const int64_t *__restrict__ seeds,
-                                                                 const int32_t *__restrict__ reverse) {
+__global__ void __launch_bounds__(kConvoyWarps * 32) reset_kernel(Batch b, const uint8_t *__restrict__ mask,
+                                                                  const int64_t *__restrict__ seeds,
+                                                                  const int32_t *__restrict__ reverse) {
     crew_start();
-    const int e = env_index();
-    if (e >= b.count || (mask && !mask[e]) || b.status[e] != kStatusOk) return;
+    const int e = env_index_spread(b.count);
+    const bool live = e < b.count && (!mask || mask[e]) && b.status[e] == kStatusOk;
+    convoy_start(live);
+    if (!live) return;
     reset_and_write(b, e, seeds, reverse);
     settle_caps(b, e);
     report(b, e);
+    convoy_leave();
 }
 
 // Rewrites the outputs of the masked environments from their observations (after a state load).
@@ -49,13 +67,50 @@ static unsigned grid_for(int count) {
     return (unsigned)((count + kThreadsPerBlock - 1) / kThreadsPerBlock);
 }
 
+// The SM count of the current device, looked up once per device.
+static cudaError_t sm_count(int *out) {
+    static std::atomic<int> cached[kStaticScratchDevices];
+    int device = -1;
+    cudaError_t rc = cudaGetDevice(&device);
+    if (rc != cudaSuccess) return rc;
+    if (device < 0 || device >= kStaticScratchDevices) return cudaErrorInvalidDevice;
+    int n = cached[device].load(std::memory_order_acquire);
+    if (n <= 0) {
+        rc = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        if (rc != cudaSuccess) return rc;
+        cached[device].store(n, std::memory_order_release);
+    }
+    *out = n;
+    return cudaSuccess;
+}
+
+// Convoy geometry: one block per SM while the batch has at most kConvoyWarps warps per SM (148
+// blocks of 3 or 4 warps for 16,384 environments on a B200), blocks of kConvoyWarps warps beyond.
+static cudaError_t convoy_geometry(int count, dim3 &grid, dim3 &block) {
+    int sms = 0;
+    cudaError_t rc = sm_count(&sms);
+    if (rc != cudaSuccess) return rc;
+    const int warps = (count + 31) / 32;
+    int blocks = (warps + kConvoyWarps - 1) / kConvoyWarps;
+    if (blocks < sms) blocks = warps < sms ? warps : sms;
+    grid = dim3((unsigned)blocks);
+    block = dim3((unsigned)(32 * ((warps + blocks - 1) / blocks)));
+    return cudaSuccess;
+}
+
 cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream) {
-    step_kernel<<<grid_for(b.count), kThreadsPerBlock, 0, stream>>>(b, actions);
+    dim3 grid, block;
+    cudaError_t rc = convoy_geometry(b.count, grid, block);
+    if (rc != cudaSuccess) return rc;
+    step_kernel<<<grid, block, 0, stream>>>(b, actions);
     return cudaGetLastError();
 }
 cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse,
                          cudaStream_t stream) {
-    reset_kernel<<<grid_for(b.count), kThreadsPerBlock, 0, stream>>>(b, mask, seeds, reverse);
+    dim3 grid, block;
+    cudaError_t rc = convoy_geometry(b.count, grid, block);
+    if (rc != cudaSuccess) return rc;
+    reset_kernel<<<grid, block, 0, stream>>>(b, mask, seeds, reverse);
     return cudaGetLastError();
 }
 cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t stream) {

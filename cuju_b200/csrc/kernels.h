@@ -7,9 +7,11 @@
 
 namespace cb {
 
-// Two warps (64 environments) per block: small blocks keep the tail of a batch short and let the
-// scheduler fill every SM with the register budget the kernels need.
+// The output kernel's block: two warps (64 environments).
 constexpr int kThreadsPerBlock = 64;
+// The step and reset kernels' blocks hold at most this many warps: one block per SM, whose warps
+// move through a tick as a convoy (crew.cuh).
+constexpr int kConvoyWarps = 4;
 
 cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream);
 cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse,

@@ -67,8 +67,10 @@ CB_HDNI bool team_process(const Sim &s, int teamID) {
         if ((m.actualTime_ms + off + 100) % 400 == 0) team_man_marking(s, teamID);
         if (*s.status) return false;
     }
-    for (int p = 0; p < m.playerCount; p++)
+    for (int p = 0; p < m.playerCount; p++) {
+        convoy_waypoint(1 + team_slot(w, teamID) * 64 + p * 2);
         if (w.playerTeamID[p] == teamID && m.players[p].base.isActive && !player_process(s, p)) return false;
+    }
     if (m.inPlay) {
         for (int g = 0; g < team.gamers.count; g++) {
             HumanGamer &gm = team.gamers.el[g];
@@ -438,6 +440,7 @@ CB_HDNI bool match_fetch_put_buffers(const Sim &s) {
 
 /// match_process.h:362 (GameTaskProcessPhase): one 10 ms tick.
 CB_HDNI bool game_tick(const Sim &s) {
+    convoy_tick();
     bool process = match_process(s);
     if (*s.status) return false;
     update_camera(s);

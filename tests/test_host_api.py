@@ -645,3 +645,40 @@ def test_a_difficulty_set_between_episodes_applies_from_the_next_reset(host_libr
     finally:
         for b in batches:
             b.close()
+
+
+def test_a_capped_loop_ends_the_step_with_the_undefined_path_error(host_library):
+    """A state whose match generator has an empty range (minimum equal to maximum, which no valid
+    state holds) makes Boost's uniform-float redraw loop run to its cap on the next draw: the loop
+    gives up, the environment's status records a path GRF leaves undefined, and the step returns an
+    error that the Python layer raises as UndefinedPathError. The other environment keeps its state.
+    The reference's own loop never ends on such a state, so it is not run here."""
+    import struct
+
+    from cuju_b200.errors import UndefinedPathError, from_library
+    from oracle.driver import OracleBatch
+
+    paths, counts = resolve('5_vs_5_l4_r0')
+    batch = OracleBatch(paths, counts, 2, 7, ANIMATIONS, threads=1, library=host_library)
+    try:
+        batch.reset()
+        for _ in range(3):
+            batch.step([0] * (2 * batch.agents))
+        engine, episode = batch.engine_state(0)
+        healthy = batch.engine_state(1)
+        # The match generator's bytes start at byte 8 of the engine state: 624 words, a 64-bit
+        # index, then the range's minimum and maximum floats (0 and 1 in every valid state).
+        at = 8 + 624 * 4 + 8
+        assert struct.unpack_from('<ff', engine, at) == (0.0, 1.0)
+        broken = engine[:at] + struct.pack('<ff', 1.0, 1.0) + engine[at + 8:]
+        batch.set_state(0, broken, episode)
+        rc, message = 0, ''
+        for _ in range(20):
+            rc, message = batch.step_status([0] * (2 * batch.agents))
+            if rc:
+                break
+        assert rc == -1
+        assert isinstance(from_library(message), UndefinedPathError), message
+        assert batch.engine_state(1) != healthy  # the healthy environment stepped on
+    finally:
+        batch.close()
