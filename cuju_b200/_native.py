@@ -94,6 +94,9 @@ def declare(library: ctypes.CDLL) -> ctypes.CDLL:
     # This build's own extension; the reference libraries that the same declarations serve lack it.
     if hasattr(library, 'cuju_b200_environment_reset_masked_device'):
         library.cuju_b200_environment_reset_masked_device.argtypes = [p, p, p, p]
+    if hasattr(library, 'cuju_b200_environment_set_lanes'):
+        library.cuju_b200_environment_set_lanes.argtypes = [p, i]
+        library.cuju_b200_environment_set_lanes.restype = i
     if hasattr(library, 'cuju_b200_environment_step_static'):
         library.cuju_b200_environment_step_static.argtypes = [p, p, p]
         library.cuju_b200_environment_step_static.restype = i

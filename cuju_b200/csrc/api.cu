@@ -261,6 +261,7 @@ public:
         b.cores = alloc<EnvCore>(c.count);
         b.slots = alloc<EnvSlot>(c.count);
         b.scratch = alloc<WarpScratch>(c.count);
+        if (!estimate) check(default_crew_log2(c.count, &b.crewLog2), "launch geometry");
         b.status = alloc<int32_t>(c.count);
         b.anyFail = alloc<int32_t>(1);
         b.reward = alloc<float>((size_t)c.count * agents);
@@ -793,6 +794,22 @@ int cuju_b200_environment_reset_masked_device(void *env, const unsigned char *ma
     try {
         static_cast<BatchEnv *>(env)->reset_masked_device(mask, reinterpret_cast<const int64_t *>(seeds),
                                                           as_stream(stream));
+        return 0;
+    } catch (const std::exception &e) {
+        return fail(e);
+    }
+}
+int cuju_b200_environment_set_lanes(void *env, int lanes) {
+    try {
+        BatchEnv &batch = *static_cast<BatchEnv *>(env);
+        int log2 = -1;
+        for (int k = 0; k <= 5; k++)
+            if (lanes == (1 << k)) log2 = k;
+        if (lanes == 0) cb::host::check(cb::default_crew_log2(batch.b.count, &log2), "launch geometry");
+        if (log2 < 0)
+            throw std::invalid_argument("expected 0 (the default) or 1, 2, 4, 8, 16 or 32 lanes per environment, found " +
+                                        std::to_string(lanes));
+        batch.b.crewLog2 = log2;
         return 0;
     } catch (const std::exception &e) {
         return fail(e);

@@ -78,6 +78,8 @@ __device__ __forceinline__ T crew_fetch(const T &v, int src) {
     return r;
 }
 #else
+CB_HD int crew_log2() { return 0; }
+CB_HD void crew_set(int) {}
 CB_HD int crew_width() { return 1; }
 CB_HD int crew_rank() { return 0; }
 CB_HD bool crew_serial() { return true; }
@@ -206,64 +208,6 @@ CB_HD void crew_copy(T &dst, const T &src) {
     static_assert(sizeof(T) % 4 == 0, "words");
     crew_copy_words(reinterpret_cast<uint32_t *>(&dst), reinterpret_cast<const uint32_t *>(&src),
                     (int)(sizeof(T) / 4));
-}
-
-// ---------------------------------------------------------------------------------------------
-// Convoys. The step is bound by the SM's instruction cache: the kernel is megabytes of code, and
-// warps of one SM that run different parts of it evict each other's lines. So the warps of a block
-// (the launch puts one block of up to four warps on each SM) move through a tick together: at a
-// waypoint (the start of a tick, of each player's turn, of a humanoid's interrupt branch) a warp
-// whose 32 lanes arrive together waits, for at most kConvoySpins naps, until every lane of the
-// block's other warps has reached that point of its own match or finished its call. A lane's
-// place is a key: ticks run in this call, then the waypoint's rank within the tick. The waits
-// change nothing a match computes; they only decide when a warp issues its next instruction.
-constexpr unsigned kConvoyDone = 0xffffffffu;
-constexpr int kConvoySpins = 2000;
-constexpr unsigned kConvoyNapNs = 100;
-__device__ __forceinline__ unsigned *convoy_keys() {
-    __shared__ unsigned keys[kCrewSlots];
-    return keys;
-}
-__device__ __forceinline__ unsigned *convoy_ticks() {
-    __shared__ unsigned ticks[kCrewSlots];
-    return ticks;
-}
-// Every thread of the block calls this once, before any returns: lanes without an environment
-// count as finished.
-__device__ __forceinline__ void convoy_start(bool live) {
-    convoy_keys()[threadIdx.x] = live ? 0u : kConvoyDone;
-    convoy_ticks()[threadIdx.x] = 0;
-    __syncthreads();
-}
-__device__ __forceinline__ void convoy_leave() { ((volatile unsigned *)convoy_keys())[threadIdx.x] = kConvoyDone; }
-// A waypoint of rank `rank` (1-255, increasing through a tick).
-CB_HD void convoy_waypoint(unsigned rank) {
-#if CB_DEVICE_PASS && __CUDA_ARCH__ >= 800
-    if (!crew_owns_env()) return;
-    volatile unsigned *keys = convoy_keys();
-    const unsigned key = (convoy_ticks()[threadIdx.x] << 8) | rank;
-    keys[threadIdx.x] = key;
-    if (__activemask() != 0xffffffffu) return;
-    const unsigned mine = __reduce_min_sync(0xffffffffu, key);
-    const int w = (int)(threadIdx.x >> 5), warps = (int)(blockDim.x >> 5), l = lane_id();
-    for (int spin = 0; spin < kConvoySpins; spin++) {
-        bool behind = false;
-        for (int o = 0; o < warps; o++)
-            if (o != w && keys[o * 32 + l] < mine) behind = true;
-        if (!__any_sync(0xffffffffu, behind)) break;
-        __nanosleep(kConvoyNapNs);
-    }
-#else
-    (void)rank;
-#endif
-}
-// The start of a tick.
-CB_HD void convoy_tick() {
-#if CB_DEVICE_PASS && __CUDA_ARCH__ >= 800
-    if (!crew_owns_env()) return;
-    convoy_ticks()[threadIdx.x]++;
-    convoy_waypoint(0);
-#endif
 }
 
 }  // namespace cb

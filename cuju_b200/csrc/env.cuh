@@ -615,6 +615,7 @@ struct Batch {
     uint8_t *done;                      // [count]
     int32_t *scoreReward;               // [count]
     const float *teamDifficulty;        // [count][2], negative for the scenario's, or null
+    int crewLog2;                       // log2 of the lanes that run each environment (0 to 5)
 };
 
 CB_HD int variant_of(const EnvSlot &s) { return s.bundle * 4 + s.reverse * 2 + ((s.episode - 1 + s.episodeOffset) & 1); }

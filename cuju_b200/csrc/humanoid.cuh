@@ -556,9 +556,7 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
         if (mayRequeue) h.interruptAnim = kIntReQueue;
     }
     convoy_waypoint(2 + team_slot(w, teamID) * 64 + p * 2);
-    if (!crew_assist(s, p, h.interruptAnim != kIntNone,
-                       [](const Sim &sim, int player) { return humanoid_interrupt(sim, player); }))
-        return false;
+    if (!crew_assist(s, kJobInterrupt, p, h.interruptAnim != kIntNone)) return false;
     h.requeueDelayFrames = h.requeueDelayFrames - 1 > 0 ? h.requeueDelayFrames - 1 : 0;
     h.interruptAnim = kIntNone;
     const Anim &a = s.A(ca.anim);
@@ -577,9 +575,7 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
     bool ctrlColl = pl.triggerControlledBallCollision;
     if (ctrlColl) pl.triggerControlledBallCollision = false;
     const bool touches = (ctrlColl && ca.touchFrame == -1) || ca.touchFrame == ca.frameNumber || w.m.ballRetainer == p;
-    if (!crew_assist(s, p | (ctrlColl ? 0x10000 : 0), touches,
-                       [](const Sim &sim, int touchArg) { return humanoid_touches(sim, touchArg); }))
-        return false;
+    if (!crew_assist(s, kJobTouches, p | (ctrlColl ? 0x10000 : 0), touches)) return false;
     const int eff = a.frameCount - 1;
     if (ca.touchFrame != -1 && ca.frameNumber <= ca.touchFrame) {
         float v = lm::lm_cosf((ca.frameNumber / (float)(ca.touchFrame + 1) - 0.5f) * kPi * 2.0f) + 1.0f;

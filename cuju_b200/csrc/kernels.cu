@@ -28,9 +28,17 @@ __device__ __forceinline__ int env_index_spread(int count) {
     return (k * base + (k < extra ? k : extra) + w) * 32 + lane_id();
 }
 
+// The environment of this thread: crews of one spread over the blocks, or one crew of
+// 2^crewLog2 lanes per environment in blocks of kConvoyWarps warps.
+__device__ __forceinline__ int env_index_for(const Batch &b) {
+    if (b.crewLog2 == 0) return env_index_spread(b.count);
+    crew_set(b.crewLog2);
+    return (int)((blockIdx.x * blockDim.x + threadIdx.x) >> b.crewLog2);
+}
+
 __global__ void __launch_bounds__(kConvoyWarps * 32) step_kernel(Batch b, const int32_t *__restrict__ actions) {
     crew_start();
-    const int e = env_index_spread(b.count);
+    const int e = env_index_for(b);
     const bool live = e < b.count && b.status[e] == kStatusOk;
     convoy_start(live);
     if (!live) return;
@@ -45,7 +53,7 @@ __global__ void __launch_bounds__(kConvoyWarps * 32) reset_kernel(Batch b, const
                                                                   const int64_t *__restrict__ seeds,
                                                                   const int32_t *__restrict__ reverse) {
     crew_start();
-    const int e = env_index_spread(b.count);
+    const int e = env_index_for(b);
     const bool live = e < b.count && (!mask || mask[e]) && b.status[e] == kStatusOk;
     convoy_start(live);
     if (!live) return;
@@ -86,10 +94,19 @@ static cudaError_t sm_count(int *out) {
 
 // Convoy geometry: one block per SM while the batch has at most kConvoyWarps warps per SM (148
 // blocks of 3 or 4 warps for 16,384 environments on a B200), blocks of kConvoyWarps warps beyond.
-static cudaError_t convoy_geometry(int count, dim3 &grid, dim3 &block) {
+static cudaError_t convoy_geometry(int count, int crewLog2, dim3 &grid, dim3 &block) {
     int sms = 0;
     cudaError_t rc = sm_count(&sms);
     if (rc != cudaSuccess) return rc;
+    if (crewLog2 > 0) {
+        // Crews of 2^crewLog2 lanes per environment: one warp per block while the warps fit one per
+        // SM (each SM's instruction cache serves one warp), kConvoyWarps warps per block beyond.
+        const long long threads = (long long)count << crewLog2;
+        const int perBlock = (threads + 31) / 32 <= sms ? 32 : kConvoyWarps * 32;
+        grid = dim3((unsigned)((threads + perBlock - 1) / perBlock));
+        block = dim3((unsigned)perBlock);
+        return cudaSuccess;
+    }
     const int warps = (count + 31) / 32;
     int blocks = (warps + kConvoyWarps - 1) / kConvoyWarps;
     if (blocks < sms) blocks = warps < sms ? warps : sms;
@@ -100,7 +117,7 @@ static cudaError_t convoy_geometry(int count, dim3 &grid, dim3 &block) {
 
 cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream) {
     dim3 grid, block;
-    cudaError_t rc = convoy_geometry(b.count, grid, block);
+    cudaError_t rc = convoy_geometry(b.count, b.crewLog2, grid, block);
     if (rc != cudaSuccess) return rc;
     step_kernel<<<grid, block, 0, stream>>>(b, actions);
     return cudaGetLastError();
@@ -108,7 +125,7 @@ cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t str
 cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse,
                          cudaStream_t stream) {
     dim3 grid, block;
-    cudaError_t rc = convoy_geometry(b.count, grid, block);
+    cudaError_t rc = convoy_geometry(b.count, b.crewLog2, grid, block);
     if (rc != cudaSuccess) return rc;
     reset_kernel<<<grid, block, 0, stream>>>(b, mask, seeds, reverse);
     return cudaGetLastError();
@@ -154,4 +171,16 @@ cudaError_t kernel_attributes(size_t *localBytes, int *registers) {
     return cudaSuccess;
 }
 
+}  // namespace cb
+
+namespace cb {
+cudaError_t default_crew_log2(int count, int *out) {
+    int sms = 0;
+    cudaError_t rc = sm_count(&sms);
+    if (rc != cudaSuccess) return rc;
+    // A batch that leaves most warp slots empty in lane mode gives each environment a whole warp:
+    // at most kConvoyWarps warps per SM either way, and 32 lanes cut an environment's latency.
+    *out = (long long)count * 32 <= (long long)sms * kConvoyWarps * 32 ? 5 : 0;
+    return cudaSuccess;
+}
 }  // namespace cb

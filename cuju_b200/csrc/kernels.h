@@ -17,6 +17,8 @@ cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t str
 cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse,
                          cudaStream_t stream);
 cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t stream);
+// The lanes per environment (log2) a batch of `count` environments runs with unless told otherwise.
+cudaError_t default_crew_log2(int count, int *out);
 // The largest per-thread local memory and register count of the kernels.
 cudaError_t kernel_attributes(size_t *localBytes, int *registers);
 

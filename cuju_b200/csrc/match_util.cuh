@@ -9,7 +9,7 @@
 
 #include "ball.cuh"
 #include "tables.cuh"
-#include "crew.cuh"
+#include "assist.cuh"
 
 namespace cb {
 
@@ -54,109 +54,6 @@ struct List {
     }
 };
 using PlayerList = List<int, kPlayers>;
-
-// Errors a step can raise without trapping the device: recorded in the match's status word.
-enum StepStatus : int32_t {
-    kStatusOk = 0,
-    kStatusUnsupported = 1,   // a path GRF leaves undefined
-    kStatusOverflow = 2,      // a fixed-capacity list would overflow
-};
-
-// The sort scratch of one environment (global memory): bitonic pairs for a warp-wide sort, or
-// the two key/position buffers of a merge sort when one lane owns the environment.
-struct alignas(16) WarpScratch {
-    double keys[2048];
-    int16_t idx[2048];
-    int16_t list[1536];
-    double keys2[1536];
-    int16_t idx2[1536];
-};
-
-// Everything a simulation function needs: the match, its context and the warp's scratch.
-struct Sim {
-    Match &w;
-    const Context &ctx;
-    WarpScratch *scratch;
-    int32_t *status;
-    CB_HD MatchState &m() const { return w.m; }
-    CB_HD const AnimTables &T() const { return *ctx.anim; }
-    CB_HD const Anim &A(int i) const { return ctx.anim->anims[i]; }
-    CB_HD const AnimDerived &D(int i) const { return ctx.anim->derived[i]; }
-    CB_HD bool fail(int32_t code) const {
-        if (*status == kStatusOk) *status = code;
-        return false;
-    }
-};
-
-// Runs fn(sim, arg) for the environment of every lane whose `need` is set, and returns the calling
-// lane's result (true where not needed). When the 32 lanes of a warp of crews of one reach the call
-// together, the k environments that need it are dealt to crews: c crews of 32/c lanes, c the
-// smallest power of two at least k (at most kAssistCrewsMax), in rounds of c environments. Each
-// crew runs fn for its environment and divides the wide loops inside (animation filters, candidate
-// sorts, ball prediction scans) between its lanes, instead of one lane running them while the
-// others wait. Otherwise every lane makes its own call. `fn` must read and write only device memory
-// reachable from the Sim it is given, never the calling lane's locals. The result and any
-// iteration-cap mark of an environment go back to the lane that owns it.
-constexpr int kAssistCrewsMax = 4;
-
-template <class Fn>
-CB_HD bool crew_assist(const Sim &s, int arg, bool need, Fn fn) {
-#if CB_DEVICE_PASS
-    if (crew_owns_env() && __activemask() == 0xffffffffu) {
-        const unsigned full = 0xffffffffu;
-        const unsigned pending = __ballot_sync(full, need);
-        if (!pending) return true;
-        const int k = __popc(pending);
-        int log2c = 0;
-        while ((1 << log2c) < k && (1 << log2c) < kAssistCrewsMax) log2c++;
-        const int crews = 1 << log2c, log2w = 5 - log2c, width = 1 << log2w;
-        const unsigned widthBits = width == 32 ? full : (1u << width) - 1u;
-        const int lane = lane_id();
-        const int crew = lane >> log2w;
-        const int myPlace = __popc(pending & ((1u << lane) - 1u));
-        const bool ownCap = crew_cap_reached();
-        bool mine = true, myCap = false;
-        for (int first = 0; first < k; first += crews) {
-            // The environment this lane's crew runs in this round: the (first + crew)-th that needs it.
-            const int place = first + crew;
-            unsigned rest = pending;
-            for (int i = 0; i < place && rest; i++) rest &= rest - 1;
-            const int src = place < k ? __ffs(rest) - 1 : lane;
-            Match *wp = reinterpret_cast<Match *>(
-                __shfl_sync(full, reinterpret_cast<unsigned long long>(&s.w), src));
-            const Context *cp = reinterpret_cast<const Context *>(
-                __shfl_sync(full, reinterpret_cast<unsigned long long>(&s.ctx), src));
-            WarpScratch *sp = reinterpret_cast<WarpScratch *>(
-                __shfl_sync(full, reinterpret_cast<unsigned long long>(s.scratch), src));
-            int32_t *stp = reinterpret_cast<int32_t *>(
-                __shfl_sync(full, reinterpret_cast<unsigned long long>(s.status), src));
-            const int a = __shfl_sync(full, arg, src);
-            __syncwarp(full);
-            crew_clear_cap();
-            bool r = true;
-            if (place < k) {
-                crew_set(log2w);
-                const Sim shared{*wp, *cp, sp, stp};
-                r = fn(shared, a);
-                crew_set(0);
-            }
-            __syncwarp(full);
-            const unsigned caps = __ballot_sync(full, crew_cap_reached());
-            const bool served = need && myPlace >= first && myPlace < first + crews;
-            const int from = served ? (myPlace - first) << log2w : lane;
-            const int got = __shfl_sync(full, (int)r, from);
-            if (served) {
-                mine = got != 0;
-                myCap = ((caps >> from) & widthBits) != 0;
-            }
-        }
-        crew_clear_cap();
-        if (ownCap || myCap) crew_note_cap();
-        return mine;
-    }
-#endif
-    return need ? fn(s, arg) : true;
-}
 
 // ---------------------------------------------------------------------------------------------
 // Teams and humanoids. A team ID is 0/1 (scenario left/right); its slot is its place in

@@ -308,9 +308,7 @@ CB_HDNI bool official_process(const Sim &s, int official) {
     ca.frameNumber++;
     h.prevAnimFrameNumber++;
     if (ca.frameNumber == s.A(ca.anim).frameCount - 1 && h.interruptAnim == kIntNone) h.interruptAnim = kIntSwitch;
-    if (!crew_assist(s, official, h.interruptAnim != kIntNone,
-                       [](const Sim &sim, int o) { return official_interrupt(sim, o); }))
-        return false;
+    if (!crew_assist(s, kJobOfficialInterrupt, official, h.interruptAnim != kIntNone)) return false;
     h.requeueDelayFrames = (int)clampf_((float)(h.requeueDelayFrames - 1), 0, 10000);
     h.interruptAnim = kIntNone;
     const Anim &pa = s.A(ca.anim);
@@ -331,6 +329,16 @@ CB_HDNI bool official_process(const Sim &s, int official) {
     for (int i = 0; i < kBodyParts; i++) h.applyBuffer.offsets[i] = h.offsets[i];
     return true;
 }
+// The branches the warps of a block share through the assist pool (assist.cuh).
+CB_HDNI bool assist_job(const Sim &s, int kind, int arg) {
+    switch (kind) {
+        case kJobInterrupt: return humanoid_interrupt(s, arg);
+        case kJobTouches: return humanoid_touches(s, arg);
+        case kJobOfficialInterrupt: return official_interrupt(s, arg);
+        default: return s.fail(kStatusUnsupported);
+    }
+}
+
 CB_HD bool officials_process(const Sim &s) {
     for (int o = 0; o < 3; o++)
         if (!official_process(s, o)) return false;

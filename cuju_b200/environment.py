@@ -141,6 +141,7 @@ class BatchEnvironment:
         episode_number: int = 0,
         first_index: int = 0,
         channel_dimensions: tuple[int, int] = (96, 72),
+        lanes_per_environment: int | None = None,
     ):
         if representation not in _REPRESENTATIONS:
             raise ChoiceError(f'expected one of {sorted(_REPRESENTATIONS)}, found {representation!r}')
@@ -198,6 +199,8 @@ class BatchEnvironment:
             raise from_library(self._library.cuju_last_error().decode())
         self._native_handle = handle
         self.environment_count = environment_count
+        if lanes_per_environment is not None:
+            self.set_lanes_per_environment(lanes_per_environment)
         left = (ctypes.c_int * environment_count)()
         right = (ctypes.c_int * environment_count)()
         self.agents = self._library.cuju_environment_agents(handle, left, right)
@@ -430,6 +433,12 @@ class BatchEnvironment:
         with torch.cuda.device(self._torch_device):
             self._check(self._library.cuju_environment_set_stack(
                 self._handle, index, b'simple115', ctypes.c_char_p(data), len(data)))
+
+    def set_lanes_per_environment(self, lanes: int) -> None:
+        """How many lanes of a warp run each environment from the next call: 1, 2, 4, 8, 16 or 32,
+        or 0 for the library's choice by batch size. This build's extension (no reference
+        counterpart); every layout gives the same results."""
+        self._check(self._library.cuju_b200_environment_set_lanes(self._handle, int(lanes)))
 
     def episode(self, index: int) -> list[int]:
         values = (ctypes.c_longlong * 17)()

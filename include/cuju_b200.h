@@ -118,6 +118,13 @@ int cuju_b200_environment_step_static(void *environment, const int *actions, voi
  * reason in cuju_last_error. */
 int cuju_b200_environment_reset_masked_device(void *environment, const unsigned char *mask, const long long *seeds,
                                               void *stream);
+/* No reference counterpart. How many lanes of a warp run each environment: 1 (each lane its own
+ * environment; a warp's 32 lanes share the long branches through the block's assist pool), 2, 4, 8,
+ * 16 or 32 (each environment a crew of that many lanes, which divide its wide loops), or 0 for the
+ * default (32 when the batch fills at most four warps per SM in that layout, else 1). Results are
+ * the same bits in every layout; only speed differs. Applies from the next launch. Returns 0, or -1
+ * with the reason in cuju_last_error. */
+int cuju_b200_environment_set_lanes(void *environment, int lanes);
 /* state_api.h:21; 1 in `mask` at the padding bytes GRF saves uninitialized, 0 elsewhere */
 int cuju_state_padding(const char *bytes, unsigned long long size, unsigned char *mask);
 /* state_api.h:51 and :86 (the reference's in-memory state layout and a gather over it); this

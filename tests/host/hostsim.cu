@@ -59,6 +59,7 @@ cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t) {
     return cudaSuccess;
 }
 cudaError_t kernel_attributes(size_t *l, int *r) { *l = 0; *r = 0; return cudaSuccess; }
+cudaError_t default_crew_log2(int, int *out) { *out = 0; return cudaSuccess; }
 cudaError_t static_scratch_address(WarpScratch **out) { *out = nullptr; return cudaErrorNotSupported; }
 }
 extern "C" __attribute__((visibility("default"))) const char *cuju_backend() { return "cpu"; }

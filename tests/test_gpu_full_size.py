@@ -1,9 +1,9 @@
 """GPU parity at sizes where the lanes of every warp are all busy.
 
-The kernels run one environment per lane and, when all 32 lanes of a warp reach a humanoid's
-command request, animation selection or ball touch together, run that branch with the whole warp
-for one environment at a time. Batches smaller than a warp never take that path, so these tests
-use full warps: a 64-environment 11v11 batch compared step by step with the reference CPU backend,
+Large batches run one environment per lane and, when all 32 lanes of a warp reach a humanoid's
+command request, animation selection or ball touch together, deal that branch to crews of the warp.
+Batches smaller than a warp never take that path, so these tests use full warps: a 64-environment
+11v11 batch on a lane per environment compared step by step with the reference CPU backend,
 and the bench workload itself (16,384 environments) with a sample of its environments compared
 against single-environment reference batches. The seed rule makes environment i identical in
 any batch that holds it (`first_index` = i for a batch of one), so the sample checks the full-size
@@ -34,7 +34,7 @@ def test_11v11_full_warps_against_the_oracle():
 
     envs, steps = 64, 40
     paths, counts = resolve(ASSETS)
-    mine = BatchEnvironment(ASSETS, environment_count=envs, seed=11, difficulty=[DIFFICULTY])
+    mine = BatchEnvironment(ASSETS, environment_count=envs, seed=11, difficulty=[DIFFICULTY], lanes_per_environment=1)
     ref = OracleBatch(paths, counts, envs, 11, ANIMATIONS, threads=0, difficulty=list(DIFFICULTY) * envs)
     try:
         generator = torch.Generator().manual_seed(3)

@@ -26,19 +26,30 @@ def test_golden_digest(case):
                          **entry['options']) == entry['digest']
 
 
+@pytest.mark.parametrize('case', ['5_vs_5/simple115v2', '11_vs_11_stochastic/simple115v2', 'mixed'])
+def test_golden_digest_one_lane_per_environment(case):
+    """Golden cases with each environment on a lane of its own (the layout of large batches),
+    where the four lanes of a partial warp run every branch themselves."""
+    g = golden()
+    entry = g['cases'][case]
+    assert device_digest(entry['assets'], g['steps'], seed=g['seed'], environments=g['environments'],
+                         lanes_per_environment=1, **entry['options']) == entry['digest']
+
+
 def _outputs(batch):
     obs, reward, done, _, score = batch._outputs()
     return (obs.cpu().numpy().tobytes(), reward.cpu().numpy().tobytes(), done.cpu().numpy().tobytes(),
             score.cpu().numpy().tobytes())
 
 
-def _compare(assets, environments, steps, seed, actions_fn, mask_fn=None, difficulty=None, rewards='scoring'):
+def _compare(assets, environments, steps, seed, actions_fn, mask_fn=None, difficulty=None, rewards='scoring',
+             lanes=None):
     from cuju_b200 import BatchEnvironment
     from oracle.driver import OracleBatch
 
     paths, counts = resolve(assets)
     mine = BatchEnvironment(assets, environment_count=environments, seed=seed, rewards=rewards,
-                            difficulty=None if difficulty is None else [difficulty])
+                            difficulty=None if difficulty is None else [difficulty], lanes_per_environment=lanes)
     flat_difficulty = None
     if difficulty is not None:
         flat_difficulty = [(-1.0 if v is None else v) for _ in range(environments) for v in difficulty]
@@ -68,10 +79,13 @@ def _compare(assets, environments, steps, seed, actions_fn, mask_fn=None, diffic
         ref.close()
 
 
-def test_5v5_four_agents_64_environments_against_the_oracle():
+@pytest.mark.parametrize('lanes', [None, 1, 8])
+def test_5v5_four_agents_64_environments_against_the_oracle(lanes):
+    """The same batch with the library's layout for its size (a warp per environment), a lane per
+    environment (the assisted branches dealt to crews of the warp) and crews of eight lanes."""
     rng = random.Random(0)
     _compare('5_vs_5_l4_r0', 64, 200, 0,
-             lambda s, e, a: [[rng.randrange(19) for _ in range(a)] for _ in range(e)])
+             lambda s, e, a: [[rng.randrange(19) for _ in range(a)] for _ in range(e)], lanes=lanes)
 
 
 def test_11v11_difficulty_and_masked_resets_against_the_oracle():
