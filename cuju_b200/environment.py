@@ -201,6 +201,9 @@ class BatchEnvironment:
         self.environment_count = environment_count
         if lanes_per_environment is not None:
             self.set_lanes_per_environment(lanes_per_environment)
+        from . import operators
+
+        self._operator_key = operators.register(self)
         left = (ctypes.c_int * environment_count)()
         right = (ctypes.c_int * environment_count)()
         self.agents = self._library.cuju_environment_agents(handle, left, right)
@@ -339,13 +342,20 @@ class BatchEnvironment:
         return self._outputs()[0]
 
     def reset_done(self) -> None:
-        """Starts the next episode of every environment whose episode ended (auto_reset off)."""
+        """Starts the next episode of every environment whose episode ended (auto_reset off); under
+        `torch.compile` through the operator `cuju_b200::reset_done`."""
+        if torch.compiler.is_compiling():
+            torch.ops.cuju_b200.reset_done(self._operator(), self._operator_tensors())
+            return
         with torch.cuda.device(self._torch_device):
             self._check(self._library.cuju_environment_reset_done(self._handle, self._stream()))
 
     def step(self, actions: Any, synchronize: bool = True):
         """One step of every environment: returns observation, reward, done and an info dict
-        with `final_observation` and `score_reward`."""
+        with `final_observation` and `score_reward`. Under `torch.compile` the step goes through the
+        operator `cuju_b200::step` (operators.py), so the compiled graph keeps it without a break."""
+        if torch.compiler.is_compiling():
+            return self._compiled_step(actions)
         a = torch.as_tensor(actions)
         if a.dim() == 1:
             a = a.reshape(self.environment_count, -1)
@@ -353,6 +363,39 @@ class BatchEnvironment:
         with torch.cuda.device(self._torch_device):
             self._check(self._library.cuju_environment_step(
                 self._handle, a.data_ptr(), int(a.is_cuda), self._stream(), int(synchronize)))
+        obs, reward, done, final, score = self._outputs()
+        return obs, reward, done, {'final_observation': final, 'score_reward': score}
+
+    # -- the path of torch.compile (python/cuju/_batch/environment.py:983-1056) ----------------
+    def _operator_tensors(self) -> list[torch.Tensor]:
+        """The output tensors the operators declare mutated: every array of the observation and
+        of the final observation, the reward, done and score_reward."""
+        obs, reward, done, final, score = self._outputs()
+        tensors = []
+        for output in (obs, reward, done, final, score):
+            tensors += [output[k] for k in sorted(output)] if isinstance(output, dict) else [output]
+        return tensors
+
+    def _operator(self):
+        return self._operator_key
+
+    def _device_step(self, actions: torch.Tensor) -> None:
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_step(self._handle, actions.data_ptr(), 1, self._stream(), 0))
+
+    def _device_reset_done(self) -> None:
+        with torch.cuda.device(self._torch_device):
+            self._check(self._library.cuju_environment_reset_done(self._handle, self._stream()))
+
+    def _compiled_step(self, actions: Any):
+        shape = (self.environment_count, self.agents)
+        actions = torch.as_tensor(actions)
+        if actions.is_floating_point() or actions.is_complex():
+            raise TypeError(f'expected integer action indices, found {actions.dtype}')
+        if tuple(actions.shape) != shape and not (self.agents == 1 and tuple(actions.shape) == shape[:1]):
+            raise ArgumentError(f'expected actions of the shape {shape}, found {tuple(actions.shape)}')
+        actions = actions.to(self._torch_device, torch.int32).reshape(shape).contiguous()
+        torch.ops.cuju_b200.step(self._operator(), actions, self._operator_tensors())
         obs, reward, done, final, score = self._outputs()
         return obs, reward, done, {'final_observation': final, 'score_reward': score}
 
@@ -452,6 +495,10 @@ class BatchEnvironment:
         """Frees the batch; a second call does nothing, and other calls then raise ClosedError."""
         handle = self.__dict__.get('_native_handle')
         if handle:
+            if self.__dict__.get('_operator_key') is not None:
+                from . import operators
+
+                operators.unregister(self._operator_key)
             torch.cuda.synchronize(self._torch_device)
             self.__dict__.get('_views', {}).clear()
             self._native_handle = None
