@@ -178,9 +178,13 @@ cudaError_t default_crew_log2(int count, int *out) {
     int sms = 0;
     cudaError_t rc = sm_count(&sms);
     if (rc != cudaSuccess) return rc;
-    // A batch that leaves most warp slots empty in lane mode gives each environment a whole warp:
-    // at most kConvoyWarps warps per SM either way, and 32 lanes cut an environment's latency.
-    *out = (long long)count * 32 <= (long long)sms * kConvoyWarps * 32 ? 5 : 0;
+    // The widest crews that keep the batch within kConvoyWarps warps per SM: a lane per environment
+    // for 16,384 environments on 148 SMs, 4 lanes for 4,096, a warp each for 592 or fewer. Beyond
+    // about four warps per SM the instruction cache, not the lanes, limits an SM, so wider crews
+    // there only add redundant lanes.
+    int log2 = 0;
+    while (log2 < 5 && ((long long)count << (log2 + 1)) <= (long long)sms * kConvoyWarps * 32) log2++;
+    *out = log2;
     return cudaSuccess;
 }
 }  // namespace cb

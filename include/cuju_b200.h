@@ -121,7 +121,8 @@ int cuju_b200_environment_reset_masked_device(void *environment, const unsigned 
 /* No reference counterpart. How many lanes of a warp run each environment: 1 (each lane its own
  * environment; a warp's 32 lanes share the long branches through the block's assist pool), 2, 4, 8,
  * 16 or 32 (each environment a crew of that many lanes, which divide its wide loops), or 0 for the
- * default (32 when the batch fills at most four warps per SM in that layout, else 1). Results are
+ * default (the widest crews that keep the batch within four warps per SM: 1 lane for 16,384
+ * environments on a 148-SM B200, 4 for 4,096, 32 for 592 or fewer). Results are
  * the same bits in every layout; only speed differs. Applies from the next launch. Returns 0, or -1
  * with the reason in cuju_last_error. */
 int cuju_b200_environment_set_lanes(void *environment, int lanes);
