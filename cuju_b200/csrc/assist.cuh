@@ -11,8 +11,9 @@
 //   of one reach one together, the environments that need it are dealt to crews of the warp
 //   (crew.cuh), which run the branch and divide its wide loops between their lanes, instead of
 //   one lane running it while the others wait.
-// * Convoy. At a waypoint (the start of a tick, of each player's turn, of a humanoid's interrupt
-//   branch) a warp whose 32 lanes arrive together waits, a bounded number of times, until every
+// * Convoy. At a waypoint (the start of a tick, of each of its phases, of each player's turn and of
+//   a humanoid's interrupt and touch branches) a warp whose 32 lanes arrive together waits, a
+//   bounded number of times, until every
 //   lane of the block's other warps has reached that point of its own match or finished. A lane's
 //   place is a key: ticks run in this call, then the waypoint's rank within the tick.
 //
@@ -30,7 +31,7 @@ enum AssistJob { kJobInterrupt = 1, kJobTouches = 2, kJobOfficialInterrupt = 3 }
 // Runs an assisted branch for the environment of `s` (defined after the branches, in officials.cuh).
 CB_HDNI bool assist_job(const Sim &s, int kind, int arg);
 
-constexpr int kAssistCrewsMax = 4;          // crews of 8 lanes at the narrowest
+constexpr int kAssistCrewsMax = 8;          // crews of 4 lanes at the narrowest
 constexpr unsigned kConvoyDone = 0xffffffffu;
 constexpr int kConvoySpins = 2000;          // naps a waypoint waits at most
 constexpr unsigned kNapNs = 100;
@@ -117,6 +118,16 @@ CB_HD bool crew_assist(const Sim &s, int kind, int arg, bool need) {
 #endif
     return need ? assist_job(s, kind, arg) : true;
 }
+
+// Waypoint ranks, in the order a tick reaches them: the ball and referee phases, each team's turn
+// (its team AI, then per player: the turn, the interrupt branch, the touch branch), and the phases
+// after both teams. A lane skips the ranks of phases its match does not run this tick.
+constexpr unsigned kWayBallCollisions = 1, kWayBallProcess = 2, kWaySwitch = 3;
+CB_HD constexpr unsigned way_team(int slot) { return 4u + 72u * (unsigned)slot; }
+CB_HD constexpr unsigned way_player(int slot, int p, int part) { return way_team(slot) + 1u + 3u * (unsigned)p + (unsigned)part; }
+constexpr unsigned kWayOfficials = 150, kWayPossession = 151, kWayCollisions = 153, kWayCamera = 154,
+                   kWayPrepare = 155, kWayFetch = 156;
+static_assert(way_player(1, kPlayers - 1, 2) < kWayOfficials, "ranks increase through a tick");
 
 // A waypoint of rank `rank` (1-255, increasing through a tick).
 CB_HD void convoy_waypoint(unsigned rank) {

@@ -555,7 +555,7 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
         }
         if (mayRequeue) h.interruptAnim = kIntReQueue;
     }
-    convoy_waypoint(2 + team_slot(w, teamID) * 64 + p * 2);
+    convoy_waypoint(way_player(team_slot(w, teamID), p, 1));
     if (!crew_assist(s, kJobInterrupt, p, h.interruptAnim != kIntNone)) return false;
     h.requeueDelayFrames = h.requeueDelayFrames - 1 > 0 ? h.requeueDelayFrames - 1 : 0;
     h.interruptAnim = kIntNone;
@@ -575,6 +575,7 @@ CB_HDNI bool humanoid_process(const Sim &s, int p) {
     bool ctrlColl = pl.triggerControlledBallCollision;
     if (ctrlColl) pl.triggerControlledBallCollision = false;
     const bool touches = (ctrlColl && ca.touchFrame == -1) || ca.touchFrame == ca.frameNumber || w.m.ballRetainer == p;
+    convoy_waypoint(way_player(team_slot(w, teamID), p, 2));
     if (!crew_assist(s, kJobTouches, p | (ctrlColl ? 0x10000 : 0), touches)) return false;
     const int eff = a.frameCount - 1;
     if (ca.touchFrame != -1 && ca.frameNumber <= ca.touchFrame) {

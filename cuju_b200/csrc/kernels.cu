@@ -28,18 +28,21 @@ __device__ __forceinline__ int env_index_spread(int count) {
     return (k * base + (k < extra ? k : extra) + w) * 32 + lane_id();
 }
 
-// The environment of this thread: crews of one spread over the blocks, or one crew of
-// 2^crewLog2 lanes per environment in blocks of kConvoyWarps warps.
-__device__ __forceinline__ int env_index_for(const Batch &b) {
-    if (b.crewLog2 == 0) return env_index_spread(b.count);
+// The environment of this thread within a launch of `count` environments: crews of one spread
+// over the blocks, or one crew of 2^crewLog2 lanes per environment in blocks of kConvoyWarps warps.
+__device__ __forceinline__ int env_index_for(const Batch &b, int count) {
+    if (b.crewLog2 == 0) return env_index_spread(count);
     crew_set(b.crewLog2);
     return (int)((blockIdx.x * blockDim.x + threadIdx.x) >> b.crewLog2);
 }
 
-__global__ void __launch_bounds__(kConvoyWarps * 32) step_kernel(Batch b, const int32_t *__restrict__ actions) {
+// A launch steps environments [first, first + count) of the batch (one wave, below).
+__global__ void __launch_bounds__(kConvoyWarps * 32) step_kernel(Batch b, const int32_t *__restrict__ actions,
+                                                                 int first, int count) {
     crew_start();
-    const int e = env_index_for(b);
-    const bool live = e < b.count && b.status[e] == kStatusOk;
+    const int local = env_index_for(b, count);
+    const int e = first + local;
+    const bool live = local < count && b.status[e] == kStatusOk;
     convoy_start(live);
     if (!live) return;
     step_environment(b, e, actions);
@@ -48,13 +51,15 @@ __global__ void __launch_bounds__(kConvoyWarps * 32) step_kernel(Batch b, const 
     convoy_leave();
 }
 
-// Resets every environment whose mask entry is set (all for a null mask).
+// Resets every environment of [first, first + count) whose mask entry is set (all for a null mask).
 __global__ void __launch_bounds__(kConvoyWarps * 32) reset_kernel(Batch b, const uint8_t *__restrict__ mask,
                                                                   const int64_t *__restrict__ seeds,
-                                                                  const int32_t *__restrict__ reverse) {
+                                                                  const int32_t *__restrict__ reverse, int first,
+                                                                  int count) {
     crew_start();
-    const int e = env_index_for(b);
-    const bool live = e < b.count && (!mask || mask[e]) && b.status[e] == kStatusOk;
+    const int local = env_index_for(b, count);
+    const int e = first + local;
+    const bool live = local < count && (!mask || mask[e]) && b.status[e] == kStatusOk;
     convoy_start(live);
     if (!live) return;
     reset_and_write(b, e, seeds, reverse);
@@ -115,20 +120,51 @@ static cudaError_t convoy_geometry(int count, int crewLog2, dim3 &grid, dim3 &bl
     return cudaSuccess;
 }
 
-cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream) {
-    dim3 grid, block;
-    cudaError_t rc = convoy_geometry(b.count, b.crewLog2, grid, block);
+// Waves: a batch larger than kConvoyWarps warps on every SM runs as equal waves of at most that
+// many environments, one launch after another on the stream. More warps per SM than that only
+// make the SM's warps evict each other's instructions (65,536 environments in one launch ran at
+// 3.2 s a step on a B200, four launches of 16,384 at 0.59 s each), and environments do not
+// depend on each other, so the split changes no result.
+static cudaError_t wave_size(int count, int crewLog2, int *out) {
+    int sms = 0;
+    cudaError_t rc = sm_count(&sms);
     if (rc != cudaSuccess) return rc;
-    step_kernel<<<grid, block, 0, stream>>>(b, actions);
-    return cudaGetLastError();
+    const long long full = ((long long)sms * kConvoyWarps * 32) >> crewLog2;
+    if (count <= full || full <= 0) {
+        *out = count;
+        return cudaSuccess;
+    }
+    const long long waves = (count + full - 1) / full;
+    *out = (int)((count + waves - 1) / waves);
+    return cudaSuccess;
+}
+
+cudaError_t launch_step(const Batch &b, const int32_t *actions, cudaStream_t stream) {
+    int wave = 0;
+    cudaError_t rc = wave_size(b.count, b.crewLog2, &wave);
+    for (int first = 0; rc == cudaSuccess && first < b.count; first += wave) {
+        const int count = b.count - first < wave ? b.count - first : wave;
+        dim3 grid, block;
+        rc = convoy_geometry(count, b.crewLog2, grid, block);
+        if (rc != cudaSuccess) return rc;
+        step_kernel<<<grid, block, 0, stream>>>(b, actions, first, count);
+        rc = cudaGetLastError();
+    }
+    return rc;
 }
 cudaError_t launch_reset(const Batch &b, const uint8_t *mask, const int64_t *seeds, const int32_t *reverse,
                          cudaStream_t stream) {
-    dim3 grid, block;
-    cudaError_t rc = convoy_geometry(b.count, b.crewLog2, grid, block);
-    if (rc != cudaSuccess) return rc;
-    reset_kernel<<<grid, block, 0, stream>>>(b, mask, seeds, reverse);
-    return cudaGetLastError();
+    int wave = 0;
+    cudaError_t rc = wave_size(b.count, b.crewLog2, &wave);
+    for (int first = 0; rc == cudaSuccess && first < b.count; first += wave) {
+        const int count = b.count - first < wave ? b.count - first : wave;
+        dim3 grid, block;
+        rc = convoy_geometry(count, b.crewLog2, grid, block);
+        if (rc != cudaSuccess) return rc;
+        reset_kernel<<<grid, block, 0, stream>>>(b, mask, seeds, reverse, first, count);
+        rc = cudaGetLastError();
+    }
+    return rc;
 }
 cudaError_t launch_outputs(const Batch &b, const uint8_t *mask, cudaStream_t stream) {
     output_kernel<<<grid_for(b.count), kThreadsPerBlock, 0, stream>>>(b, mask);

@@ -60,6 +60,7 @@ CB_HDNI bool team_process(const Sim &s, int teamID) {
         team.fadingTeamPossessionAmount = team.teamPossessionAmount = amount;
     }
     team_gamers_select_anyone(s, teamID);
+    convoy_waypoint(way_team(team_slot(w, teamID)));
     if (m.inPlay && !m.inSetPiece) {
         if (!team_ai_process(s, teamID)) return false;
         uint64_t off = teamID == (1 - w.firstTeamID()) ? 200 : 0;
@@ -68,7 +69,7 @@ CB_HDNI bool team_process(const Sim &s, int teamID) {
         if (*s.status) return false;
     }
     for (int p = 0; p < m.playerCount; p++) {
-        convoy_waypoint(1 + team_slot(w, teamID) * 64 + p * 2);
+        convoy_waypoint(way_player(team_slot(w, teamID), p, 0));
         if (w.playerTeamID[p] == teamID && m.players[p].base.isActive && !player_process(s, p)) return false;
     }
     if (m.inPlay) {
@@ -230,6 +231,7 @@ CB_HDNI bool match_process(const Sim &s) {
     const bool rev = w.scenario.reverseTeamProcessing;
     const int first = w.firstTeamID(), second = 1 - first;
 
+    convoy_waypoint(kWayBallCollisions);
     mirror_match(w, rev, !rev, rev);
     if (m.inPlay && !check_ball_collisions(s)) return false;
     if (!referee_process(s)) return false;
@@ -239,10 +241,12 @@ CB_HDNI bool match_process(const Sim &s) {
         bump_actual_time(s, 10);
         return false;
     }
+    convoy_waypoint(kWayBallProcess);
     mirror_match(w, false, false, rev);
     ball_process(m.ball, m.ballIsInGoal);
     mirror_match(w, false, false, rev);
 
+    convoy_waypoint(kWaySwitch);
     if (m.mentalImages.count == 0 || m.actualTime_ms % 100 == 0) push_mental_image(w);
 
     if (!team_update_switch(s, first)) return false;
@@ -254,12 +258,15 @@ CB_HDNI bool match_process(const Sim &s) {
     if (!team_process(s, second)) return false;
     mirror_match(w, first == 0, first == 1, first == 0);
 
+    convoy_waypoint(kWayOfficials);
     mirror_match(w, rev, !rev, rev);
     if (!officials_process(s)) return false;
     mirror_match(w, rev, !rev, rev);
 
+    convoy_waypoint(kWayPossession);
     mirror_match(w, first == 1, first == 0, first == 1);
     team_possession_stats(s, first);
+    convoy_waypoint(kWayPossession + 1);
     mirror_match(w, true, true, true);
     team_possession_stats(s, second);
     mirror_match(w, first == 0, first == 1, first == 0);
@@ -283,6 +290,7 @@ CB_HDNI bool match_process(const Sim &s) {
         m.designatedPossessionPlayer = m.ballRetainer;
     }
 
+    convoy_waypoint(kWayCollisions);
     mirror_match(w, rev, !rev, rev);
     if (!check_humanoid_collisions(s)) return false;
     bump_actual_time(s, 10);
@@ -443,9 +451,12 @@ CB_HDNI bool game_tick(const Sim &s) {
     convoy_tick();
     bool process = match_process(s);
     if (*s.status) return false;
+    convoy_waypoint(kWayCamera);
     update_camera(s);
     if (process) {
+        convoy_waypoint(kWayPrepare);
         match_prepare_put_buffers(s);
+        convoy_waypoint(kWayFetch);
         if (!match_fetch_put_buffers(s)) return false;
     }
     return *s.status == 0;

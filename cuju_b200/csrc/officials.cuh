@@ -329,7 +329,7 @@ CB_HDNI bool official_process(const Sim &s, int official) {
     for (int i = 0; i < kBodyParts; i++) h.applyBuffer.offsets[i] = h.offsets[i];
     return true;
 }
-// The branches the warps of a block share through the assist pool (assist.cuh).
+// The branches the lanes of a warp share in assist rounds (assist.cuh: crew_assist).
 CB_HDNI bool assist_job(const Sim &s, int kind, int arg) {
     switch (kind) {
         case kJobInterrupt: return humanoid_interrupt(s, arg);

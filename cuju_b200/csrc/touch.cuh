@@ -15,6 +15,38 @@ CB_HD void ball_recalc(Match &w) {
     ball_predict_path(w.m.ball, w.m.ballIsInGoal, unused);
 }
 
+// The outcome of a second ball_recalc right after one on the same inputs (momentum, position,
+// orientation and spin buffers unchanged, no lazy mirror pending), without running the flight
+// again. Its first step lands on predictions[1] again (with the same orientation prediction and
+// net touch), so its cache test reads predictions[2] == predictions[1]. Where that holds it
+// shifts entries 2..399 down by one, as a cached run does; otherwise it recomputes every later
+// step from the same inputs, which gives back the entries already there.
+CB_HD void ball_recalc_again(Ball &b) {
+    if (!(b.validPredictions > 0 && b.predictions[2] == b.predictions[1])) {
+        b.validPredictions = (int32_t)kCachedPredictions;
+        return;
+    }
+    b.validPredictions--;
+    const int last = (int)(kPredictionSpan_ms + kCachedPredictions * 10) / 10 - 1;  // 399
+#if CB_DEVICE_PASS
+    if (!crew_serial()) {
+        // One block of entries per pass, one entry per lane: each lane reads its source before the
+        // barrier and writes one place down after it; a pass writes only below what later passes read.
+        const int w = crew_width();
+        for (int base = 2; base <= last; base += w) {
+            const int e = base + crew_rank();
+            Vec3 v;
+            if (e <= last) v = b.predictions[e + 1];
+            crew_sync();
+            if (e <= last) b.predictions[e] = v;
+            crew_sync();
+        }
+        return;
+    }
+#endif
+    for (int e = 2; e <= last; e++) b.predictions[e] = b.predictions[e + 1];
+}
+
 // One tick of the ball: predict, advance one step, append the position history (401 entries).
 CB_HDNI void ball_process(Ball &b, bool inGoal) {
     ball_materialize(b);
@@ -79,7 +111,7 @@ CB_HDNI void ball_touch(const Sim &s, const Vec3 &target) {
     if (b.positionBuffer.c[2] < 0.11f) b.positionBuffer.c[2] = 0.11f;
     b.momentum = target;
     ball_recalc(w);
-    ball_recalc(w);
+    ball_recalc_again(b);
     if (w.m.mentalImages.count > 0) {
         MentalImage &im = w.m.mentalImages[0];
         im.ballPredictions.count = kPredictionSpan_ms / 10;

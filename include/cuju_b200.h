@@ -119,7 +119,7 @@ int cuju_b200_environment_step_static(void *environment, const int *actions, voi
 int cuju_b200_environment_reset_masked_device(void *environment, const unsigned char *mask, const long long *seeds,
                                               void *stream);
 /* No reference counterpart. How many lanes of a warp run each environment: 1 (each lane its own
- * environment; a warp's 32 lanes share the long branches through the block's assist pool), 2, 4, 8,
+ * environment; a warp's 32 lanes share the long branches in assist rounds), 2, 4, 8,
  * 16 or 32 (each environment a crew of that many lanes, which divide its wide loops), or 0 for the
  * default (the widest crews that keep the batch within four warps per SM: 1 lane for 16,384
  * environments on a 148-SM B200, 4 for 4,096, 32 for 592 or fewer). Results are
