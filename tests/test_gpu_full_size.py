@@ -89,6 +89,50 @@ def test_bench_workload_sampled_environments_match_the_oracle():
             ref.close()
 
 
+def test_batch_of_several_waves_matches_the_oracle():
+    """A batch larger than four warps on every SM steps as equal waves of launches (20,000
+    environments: two of 10,000). Environments on both sides of the wave boundary, through a masked
+    reset inside the second wave, against single-environment reference batches."""
+    from cuju_b200 import BatchEnvironment
+    from oracle.driver import OracleBatch
+
+    envs, steps = 20000, 10
+    sample = [0, 31, 9999, 10000, 10001, 10031, 15000, 19999]
+    paths, counts = resolve(ASSETS)
+    mine = BatchEnvironment(ASSETS, environment_count=envs, seed=3, difficulty=[DIFFICULTY])
+    refs = {e: OracleBatch(paths, counts, 1, 3, ANIMATIONS, threads=1, difficulty=list(DIFFICULTY), first_index=e)
+            for e in sample}
+    try:
+        generator = torch.Generator().manual_seed(21)
+        mine.reset()
+        for e, ref in refs.items():
+            assert _row_bytes(mine._outputs()[0], e) == ref.reset()[0], f'reset of environment {e} differs'
+        for step in range(steps):
+            actions = torch.randint(0, 19, (envs, mine.agents), generator=generator, dtype=torch.int32)
+            mine.step(actions.cuda())
+            obs, reward, done, _, score = mine._outputs()
+            for e, ref in refs.items():
+                expected = ref.step(actions[e].tolist())
+                got = (_row_bytes(obs, e), _row_bytes(reward, e), _row_bytes(done, e), _row_bytes(score, e))
+                for name, a, b in zip(('simple115', 'reward', 'done', 'score_reward'), got, expected):
+                    assert a == b, f'{name} of environment {e} differs at step {step}'
+            if step == 4:
+                mask = torch.zeros(envs, dtype=torch.bool)
+                mask[[10001, 15000]] = True
+                seeds = torch.full((envs,), -1, dtype=torch.int64)
+                seeds[10001], seeds[15000] = 987654321, 123456789
+                mine.reset(mask=mask, seeds=seeds)
+                for e in (10001, 15000):
+                    expected = refs[e].reset_masked([1], [int(seeds[e])])
+                    assert _row_bytes(mine._outputs()[0], e) == expected[0], f'masked reset of {e} differs'
+        for e, ref in refs.items():
+            assert mine.engine_state(e)[0] == ref.engine_state(0)[0], f'state of environment {e} differs'
+    finally:
+        mine.close()
+        for ref in refs.values():
+            ref.close()
+
+
 REFERENCE_CUDA = os.path.join(ROOT, 'oracle', '_ref', 'libcuju_cuda.so')
 
 
