@@ -39,10 +39,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = 'env steps/sec, 11v11 at 1/2/4/8 B200 vs host-CPU path; % HBM roofline'
 DRILL = os.path.join(ROOT, 'tests', 'golden', 'academy_attacker_vs_keeper_l0_r0.cjb')
-# DRAM bytes (read + write) of one step_kernel launch at 16,384 environments of configuration 3,
-# from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum, one pass); None where no
-# capture covers the configuration.
-TRAFFIC_GB = {3: None}
+# DRAM bytes (read + write) of one step_kernel launch of configuration 3 in GB: one ncu capture at
+# 8,192 environments (dram__bytes_read.sum + dram__bytes_write.sum = 44.64 GB, the 4th step)
+# scaled by the environments of a 16,384-environment launch, since the traffic is per-environment
+# state and stack; None where no capture covers the configuration.
+TRAFFIC_GB = {3: 89.3}
 
 CONFIGS = {
     1: dict(assets=['5_vs_5_l4_r0'], agents=None, difficulty=(None, 0.6), envs=64, split=False, masked=0.0,
@@ -235,16 +236,34 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def make_batch(cfg: dict, envs: int, first: int, device):
+def make_batch(cfg: dict, envs: int, first: int, device, lanes: int = 0):
     from cuju_b200 import BatchEnvironment
 
     options = {}
     if cfg['agents']:
         options['agent_counts'] = cfg['agents']
+    if lanes:
+        options['lanes_per_environment'] = lanes
     return BatchEnvironment(cfg['assets'] if len(cfg['assets']) > 1 else cfg['assets'][0], environment_count=envs,
                             seed=0, device=device, difficulty=None if cfg['difficulty'] is None else [cfg['difficulty']],
                             first_index=first, assignment=assignment_of(cfg, envs, first), stacked=cfg['stacked'],
                             **options)
+
+
+def launches_per_step(envs: int, lanes: int, device) -> int:
+    """Kernel launches of one step (or one masked reset): a batch above four warps per SM runs as
+    equal waves of launches (cuju_b200/csrc/kernels.cu: wave_size, default_crew_log2)."""
+    import torch
+
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    if lanes:
+        log2 = max(0, lanes.bit_length() - 1)
+    else:
+        log2 = 0
+        while log2 < 5 and (envs << (log2 + 1)) <= sms * 4 * 32:
+            log2 += 1
+    full = (sms * 4 * 32) >> log2
+    return 1 if envs <= full else -(-envs // full)
 
 
 def bytes_per_env_step(cfg: dict, batch, envs: int, first: int) -> float:
@@ -280,7 +299,7 @@ def run_b200(args) -> None:
     envs, first = slice_of(cfg, world, rank)
     if args.envs:
         envs, first = args.envs, rank * args.envs
-    batch = make_batch(cfg, envs, first, device)
+    batch = make_batch(cfg, envs, first, device, args.lanes)
     agents = batch.agents
     generator = torch.Generator(device=device).manual_seed(1000 + rank)
     total_steps = args.warmup + args.steps
@@ -344,7 +363,7 @@ def run_b200(args) -> None:
     done_host = torch.empty((envs,), dtype=torch.bool, pin_memory=True)
     e2e_steps = max(1, min(args.steps, args.e2e_steps if args.e2e_steps else args.steps))
     batch.close()
-    batch = make_batch(cfg, envs, first, device)
+    batch = make_batch(cfg, envs, first, device, args.lanes)
     start(batch)
     for step in range(args.warmup):
         device_step(batch, step)
@@ -391,14 +410,15 @@ def run_b200(args) -> None:
             'data': 'synthetic', 'config': workload_config(args.config, envs, world),
             'e2e': {'value': e2e_value, 'unit': 'env steps/s', 'h2d_bytes_per_step': 4 * envs * agents,
                     'd2h_bytes_per_step': envs * obs_floats * 4 + envs * agents * 4 + envs},
-            'gpu_launches': args.steps * (2 if masks is not None else 1),
+            'gpu_launches': args.steps * launches_per_step(envs, args.lanes, device) * (2 if masks is not None else 1),
             'per_rank_ms_per_step': [round(x, 3) for x in rank_ms],
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s',
                          'frac': achieved / peak, 'traffic': traffic,
                          'note': f'algorithmic {per_step_bytes:.0f} B per env-step (2 x the measured GRF state size '
                                  'plus actions and outputs) x the environments of a launch over the mean CUDA-event '
                                  f'time of a step launch; peak {peak_kind} (of measured); traffic in GB per launch, '
-                                 'DRAM read+write of one ncu capture of the same launch'},
+                                 'DRAM read+write of one ncu capture at 8,192 environments scaled to this launch\'s '
+                                 'environments'},
             'clocks': clock,
         }
         if args.cpu_baseline:
@@ -421,6 +441,8 @@ def main() -> None:
     parser.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     parser.add_argument('--config', type=int, default=3, choices=sorted(CONFIGS))
     parser.add_argument('--envs', type=int, default=0, help='environments per GPU (default: the configuration\'s)')
+    parser.add_argument('--lanes', type=int, default=0,
+                        help='lanes per environment, 1-32 (default: the library\'s choice for the batch size)')
     parser.add_argument('--e2e-steps', type=int, default=0, help='end-to-end steps (default: --steps)')
     parser.add_argument('--cpu-steps', type=int, default=30)
     parser.add_argument('--no-cpu-baseline', dest='cpu_baseline', action='store_false')
