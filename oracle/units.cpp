@@ -63,3 +63,41 @@ extern "C" __attribute__((visibility("default"))) float oracle_modulate_into_ran
                                                                                   float value) {
     return cuju::ModulateIntoRange(min, max, value);
 }
+
+// oracle_libm: the reference's restatements of glibc's math functions (cuju include/cuju/libm/*.h),
+// `n` evaluations of function `which` on x (and y for the two-argument ones), each result widened
+// to double. Functions: 0 sinf, 1 cosf, 2 powf, 3 acosf, 4 asinf, 5 atanf, 6 atan2f, 7 sin, 8 cos,
+// 9 acos, 10 pow; 11, 12 and 13 are sinf, cosf and powf again (the checks of the library's
+// sine-and-cosine pair and of its positive-base power).
+#include "cuju/libm/acos_double.h"
+#include "cuju/libm/asinf.h"
+#include "cuju/libm/inverse_trigonometric_float.h"
+#include "cuju/libm/pow.h"
+#include "cuju/libm/powf.h"
+#include "cuju/libm/sin_double.h"
+#include "cuju/libm/sincosf.h"
+
+extern "C" __attribute__((visibility("default"))) int oracle_libm(int which, const double *x, const double *y,
+                                                                 double *out, int n) {
+    for (int i = 0; i < n; i++) {
+        const float xf = (float)x[i], yf = (float)y[i];
+        switch (which) {
+            case 0: out[i] = cuju::libm::sinf(xf); break;
+            case 1: out[i] = cuju::libm::cosf(xf); break;
+            case 2: out[i] = cuju::libm::powf(xf, yf); break;
+            case 3: out[i] = cuju::libm::acosf(xf); break;
+            case 4: out[i] = cuju::libm::asinf(xf); break;
+            case 5: out[i] = cuju::libm::atanf(xf); break;
+            case 6: out[i] = cuju::libm::atan2f(yf, xf); break;
+            case 7: out[i] = cuju::libm::sin(x[i]); break;
+            case 8: out[i] = cuju::libm::cos(x[i]); break;
+            case 9: out[i] = cuju::libm::acos(x[i]); break;
+            case 10: out[i] = cuju::libm::pow(x[i], y[i]); break;
+            case 11: out[i] = cuju::libm::sinf(xf); break;
+            case 12: out[i] = cuju::libm::cosf(xf); break;
+            case 13: out[i] = cuju::libm::powf(xf, yf); break;
+            default: return -1;
+        }
+    }
+    return 0;
+}

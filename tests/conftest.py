@@ -132,3 +132,89 @@ def host_library(tmp_path_factory):
                     '-I', os.path.join(ROOT, 'cuju_b200', 'csrc'), '-shared',
                     os.path.join(ROOT, 'tests', 'host', 'hostsim.cu'), '-o', out], check=True, capture_output=True)
     return out
+
+
+LIBM_NAMES = {0: 'sinf', 1: 'cosf', 2: 'powf', 3: 'acosf', 4: 'asinf', 5: 'atanf', 6: 'atan2f', 7: 'sin', 8: 'cos',
+              9: 'acos', 10: 'pow', 11: 'sincosf sine', 12: 'sincosf cosine', 13: 'powf, positive base'}
+
+
+def libm_inputs(which, count=20000):
+    """Seeded arguments (x, y) for the math function `which` (numbering of tests/host/libm_eval.cuh):
+    special values, the ranges the simulation uses, and wide magnitudes. Arguments of the float
+    functions are exactly representable floats."""
+    import math
+    import random
+    import struct
+
+    rng = random.Random(1000 + which)
+    single = which in (0, 1, 2, 3, 4, 5, 6, 11, 12, 13)
+
+    def rnd(v):
+        return struct.unpack('<f', struct.pack('<f', v))[0] if single and math.isfinite(v) and abs(v) < 3.4e38 else v
+
+    def wide(lo, hi):
+        return rng.choice((-1.0, 1.0)) * 10.0 ** rng.uniform(lo, hi)
+
+    special = [0.0, -0.0, 1.0, -1.0, 0.5, -0.5, 2.0, -2.0, math.pi / 4, math.pi / 2, math.pi, 2 ** -12, 1e-30,
+               -1e-30, 1e-42, 1e3, 1e6, 3e7, 1e20, 3e38, math.inf, -math.inf, math.nan]
+    xs, ys = [], []
+    if which in (2, 10):
+        for a in special:
+            for b in (0.0, -0.0, 1.0, -1.0, 2.0, 3.0, 0.5, -0.5, 2.5, 1e10, math.inf, -math.inf, math.nan):
+                xs.append(a)
+                ys.append(b)
+        span = (-6, 4) if which == 2 else (-8, 8)
+        for _ in range(count):
+            xs.append(10.0 ** rng.uniform(*span) * (1.0 if rng.random() < 0.9 else -1.0))
+            ys.append(rng.uniform(-8, 8) if which == 2 else rng.uniform(-20, 20))
+            if rng.random() < 0.1:
+                ys[-1] = float(round(ys[-1]))
+    elif which == 13:
+        for _ in range(count):
+            xs.append(rng.uniform(0, 1) if rng.random() < 0.7 else rng.uniform(0, 100))
+            ys.append(rng.uniform(0.05, 4))
+        xs += [0.0, 1.0, 0.0, 1.0]
+        ys += [0.7, 0.8, 1.5, 2.6]
+    elif which == 6:
+        for a in special:
+            for b in special:
+                xs.append(a)
+                ys.append(b)
+        for _ in range(count):
+            xs.append(rng.uniform(-100, 100))
+            ys.append(rng.uniform(-100, 100))
+    else:
+        xs = list(special)
+        if which in (3, 4, 9):
+            xs += [rng.uniform(-1.05, 1.05) for _ in range(count)] + [1 - 2 ** -24, -(1 - 2 ** -24)]
+        else:
+            xs += [rng.uniform(-10, 10) for _ in range(count)]
+            xs += [rng.uniform(-1e4, 1e4) for _ in range(count // 4)]
+            xs += [wide(-10, 38 if single else 300) for _ in range(count // 4)]
+        ys = [0.0] * len(xs)
+    return [rnd(v) for v in xs], [rnd(v) for v in ys]
+
+
+def libm_compare(evaluate, which, xs, ys):
+    """Evaluates the library's and the reference's function on the same arguments and returns the
+    first argument pair whose results differ in any bit (any NaN equals any NaN), or None."""
+    import ctypes
+    import math
+    import struct
+
+    units_path = os.path.join(ROOT, 'oracle', '_ref', 'liboracle_units.so')
+    if not os.path.isfile(units_path):
+        pytest.skip('run make -C oracle for the unit shim')
+    units = ctypes.CDLL(units_path)
+    n = len(xs)
+    arr = ctypes.c_double * n
+    x, y, mine, ref = arr(*xs), arr(*ys), arr(), arr()
+    assert evaluate(which, x, y, mine, n) == 0
+    assert units.oracle_libm(which, x, y, ref, n) == 0
+    for i in range(n):
+        a, b = mine[i], ref[i]
+        if math.isnan(a) and math.isnan(b):
+            continue
+        if struct.pack('<d', a) != struct.pack('<d', b):
+            return xs[i], ys[i], a, b
+    return None

@@ -64,6 +64,16 @@ cudaError_t static_scratch_address(WarpScratch **out) { *out = nullptr; return c
 }
 extern "C" __attribute__((visibility("default"))) const char *cuju_backend() { return "cpu"; }
 
+#include "libm_eval.cuh"
+
+// The library's math functions on the host, for the per-function check against the reference's
+// restatements (tests/test_libm.py; numbering of libm_eval.cuh).
+extern "C" __attribute__((visibility("default"))) int hostsim_libm(int which, const double *x, const double *y,
+                                                                  double *out, int n) {
+    for (int i = 0; i < n; i++) out[i] = libm_eval(which, x[i], y[i]);
+    return 0;
+}
+
 // The device code's range wrap, for a unit check against the reference's (tests/test_host_api.py).
 extern "C" __attribute__((visibility("default"))) float hostsim_wrap_range(float lo, float hi, float v) {
     return cb::wrap_range(lo, hi, v);
