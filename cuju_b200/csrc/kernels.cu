@@ -123,8 +123,8 @@ static cudaError_t convoy_geometry(int count, int crewLog2, dim3 &grid, dim3 &bl
 // Waves: a batch larger than kConvoyWarps warps on every SM runs as equal waves of at most that
 // many environments, one launch after another on the stream. More warps per SM than that only
 // make the SM's warps evict each other's instructions (65,536 environments in one launch ran at
-// 3.2 s a step on a B200, four launches of 16,384 at 0.59 s each), and environments do not
-// depend on each other, so the split changes no result.
+// 3.2 s a step on a B200, in four launches of 16,384 at 2.2 s), and environments do not depend on
+// each other, so the split changes no result.
 static cudaError_t wave_size(int count, int crewLog2, int *out) {
     int sms = 0;
     cudaError_t rc = sm_count(&sms);
