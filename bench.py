@@ -423,10 +423,15 @@ def run_b200(args) -> None:
         }
         if args.cpu_baseline:
             threads = host_threads()
-            cpu = cpu_reference(args.config, reference_envs(args.config, threads), args.cpu_steps, 2, threads)
+            # The same match phase as the timed device steps: the same warm-up, then as many steps
+            # (a step's cost grows as the matches get going after kick-off).
+            cpu_steps = args.cpu_steps or args.steps
+            cpu_warmup = max(1, args.warmup)
+            cpu = cpu_reference(args.config, reference_envs(args.config, threads), cpu_steps, cpu_warmup, threads)
             line['cpu_baseline'] = {'value': cpu['value'], 'unit': 'env steps/s', 'cores': threads,
                                     'kind': 'reference',
-                                    'sample': f"{cpu['envs']} envs x {cpu['steps']} steps of the same workload, "
+                                    'sample': f"{cpu['envs']} envs x {cpu['steps']} steps after {cpu_warmup} warm-up "
+                                              'steps of the same workload (the device line\'s match phase), '
                                               'reference CPU backend built from source'}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -444,7 +449,7 @@ def main() -> None:
     parser.add_argument('--lanes', type=int, default=0,
                         help='lanes per environment, 1-32 (default: the library\'s choice for the batch size)')
     parser.add_argument('--e2e-steps', type=int, default=0, help='end-to-end steps (default: --steps)')
-    parser.add_argument('--cpu-steps', type=int, default=30)
+    parser.add_argument('--cpu-steps', type=int, default=0, help='CPU baseline steps (default: --steps)')
     parser.add_argument('--no-cpu-baseline', dest='cpu_baseline', action='store_false')
     args = parser.parse_args()
     if args.impl == 'reference':
