@@ -421,7 +421,7 @@ def run_b200(args) -> None:
                                  'environments'},
             'clocks': clock,
         }
-        if args.cpu_baseline:
+        if args.cpu_baseline and world == 1:
             threads = host_threads()
             # The same match phase as the timed device steps: the same warm-up, then as many steps
             # (a step's cost grows as the matches get going after kick-off).
