@@ -250,12 +250,10 @@ def make_batch(cfg: dict, envs: int, first: int, device, lanes: int = 0):
                             **options)
 
 
-def launches_per_step(envs: int, lanes: int, device) -> int:
-    """Kernel launches of one step (or one masked reset): a batch above four warps per SM runs as
-    equal waves of launches (cuju_b200/csrc/kernels.cu: wave_size, default_crew_log2)."""
-    import torch
-
-    sms = torch.cuda.get_device_properties(device).multi_processor_count
+def waves_for(envs: int, lanes: int, sms: int) -> int:
+    """Kernel launches of one step (or one masked reset) of `envs` environments on `sms` SMs: a
+    batch above four warps per SM runs as equal waves of launches. Mirrors the library's choice
+    (cuju_b200/csrc/kernels.cu: default_crew_log2, wave_size); `lanes` 0 is its default layout."""
     if lanes:
         log2 = max(0, lanes.bit_length() - 1)
     else:
@@ -264,6 +262,12 @@ def launches_per_step(envs: int, lanes: int, device) -> int:
             log2 += 1
     full = (sms * 4 * 32) >> log2
     return 1 if envs <= full else -(-envs // full)
+
+
+def launches_per_step(envs: int, lanes: int, device) -> int:
+    import torch
+
+    return waves_for(envs, lanes, torch.cuda.get_device_properties(device).multi_processor_count)
 
 
 def bytes_per_env_step(cfg: dict, batch, envs: int, first: int) -> float:
