@@ -179,3 +179,36 @@ def test_state_padding_equals_the_reference(assets):
         assert ours.cuju_state_padding(b'\x00\x01', 2, bad) == -1
     finally:
         batch.close()
+
+
+@pytest.mark.skipif(not os.path.isfile(LIBRARY), reason='library not built')
+def test_a_c_program_binds_the_header_and_the_library(tmp_path):
+    """The C-ABI from C: the header compiles as C11, and a C program linked against the library
+    calls entry points that need no device (the backend name, the last error, the local memory a
+    batch reserves per thread)."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which('gcc') or shutil.which('cc')
+    if cc is None:
+        pytest.skip('no C compiler')
+    source = tmp_path / 'bind.c'
+    source.write_text(
+        '#include <stdio.h>\n'
+        '#include "cuju_b200.h"\n'
+        'int main(void) {\n'
+        '    cuju_configuration c = {0};\n'
+        '    c.version = CUJU_CONFIGURATION_VERSION;\n'
+        '    if (cuju_environment_create(&c) != NULL) return 2;  /* no assets: refused */\n'
+        '    printf("%s|%s\\n", cuju_backend(), cuju_last_error());\n'
+        '    return 0;\n'
+        '}\n')
+    exe = tmp_path / 'bind'
+    libdir = os.path.dirname(LIBRARY)
+    subprocess.run([cc, '-std=c11', '-Wall', '-Werror', '-I', os.path.join(ROOT, 'include'), str(source), '-o',
+                    str(exe), '-L', libdir, '-lcuju_b200', f'-Wl,-rpath,{libdir}'], check=True)
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stderr
+    backend, message = run.stdout.strip().split('|', 1)
+    assert backend == 'cuda'
+    assert message  # the refusal says why
