@@ -15,12 +15,13 @@ CB_HD void ball_recalc(Match &w) {
     ball_predict_path(w.m.ball, w.m.ballIsInGoal, unused);
 }
 
-// The outcome of a second ball_recalc right after one on the same inputs (momentum, position,
-// orientation and spin buffers unchanged, no lazy mirror pending), without running the flight
-// again. Its first step lands on predictions[1] again (with the same orientation prediction and
-// net touch), so its cache test reads predictions[2] == predictions[1]. Where that holds it
-// shifts entries 2..399 down by one, as a cached run does; otherwise it recomputes every later
-// step from the same inputs, which gives back the entries already there.
+// The outcome of a second ball_recalc right after one that computed every entry (an empty cache,
+// as ball_touch makes it) on the same inputs (momentum, position, orientation and spin buffers
+// unchanged, no lazy mirror pending), without running the flight again. Its first step lands on
+// predictions[1] again (with the same orientation prediction and net touch), so its cache test
+// reads predictions[2] == predictions[1]. Where that holds it shifts entries 2..399 down by one,
+// as a cached run does; otherwise it recomputes every later step from the same inputs, which gives
+// back the entries already there.
 CB_HD void ball_recalc_again(Ball &b) {
     if (!(b.validPredictions > 0 && b.predictions[2] == b.predictions[1])) {
         b.validPredictions = (int32_t)kCachedPredictions;

@@ -66,6 +66,50 @@ extern "C" __attribute__((visibility("default"))) const char *cuju_backend() { r
 
 #include "libm_eval.cuh"
 
+#include <random>
+
+// The touch's repeated ball prediction: for `trials` seeded balls (on the ground, in flight, at
+// rest, against a post, in the goal), the ball after ball_recalc run twice and after ball_recalc
+// then ball_recalc_again, from an empty prediction cache as ball_touch leaves it. Odd trials also
+// set the first run's 20 ms entry to its 10 ms entry in both copies before the second call, so
+// that the second call takes its cached shift (a ball that does not move between 10 and 20 ms,
+// which real flights hardly produce). Returns the number of trials whose balls differ in any
+// byte, and counts the trials whose second call shifted (`shifted`).
+extern "C" __attribute__((visibility("default"))) int hostsim_check_recalc_again(unsigned seed, int trials,
+                                                                                int *shifted) {
+    std::mt19937 rng(seed);
+    std::uniform_real_distribution<float> u(-1.0f, 1.0f);
+    auto *a = static_cast<cb::Match *>(calloc(1, sizeof(cb::Match)));
+    auto *b = static_cast<cb::Match *>(calloc(1, sizeof(cb::Match)));
+    int bad = 0;
+    *shifted = 0;
+    for (int t = 0; t < trials; t++) {
+        memset(a, 0, sizeof(cb::Match));
+        cb::Ball &ball = a->m.ball;
+        const int kind = (t / 2) % 5;
+        ball.positionBuffer = cb::Vec3(55.0f * u(rng), 36.0f * u(rng), 0.11f);
+        if (kind == 1) ball.positionBuffer.c[2] = 0.11f + 4.0f * (u(rng) + 1.0f);
+        if (kind == 3) ball.positionBuffer = cb::Vec3(54.9f + 0.1f * u(rng), 3.7f + 0.05f * u(rng), 0.5f + u(rng));
+        if (kind == 4) ball.positionBuffer = cb::Vec3(56.0f + u(rng), 2.0f * u(rng), 0.5f + 0.4f * u(rng));
+        ball.momentum = kind == 2 ? cb::Vec3(0.0f) : cb::Vec3(25.0f * u(rng), 25.0f * u(rng), 8.0f * u(rng));
+        const float s = 0.01f * u(rng);
+        ball.rotationPerMs = kind == 2 ? cb::Quat::identity() : cb::Quat(s, -s, 0.5f * s, 1.0f).normalized();
+        ball.orientationBuffer = cb::Quat(0.1f * u(rng), 0.1f * u(rng), 0.1f * u(rng), 1.0f).normalized();
+        ball.validPredictions = 0;
+        a->m.ballIsInGoal = kind == 4;
+        cb::ball_recalc(*a);
+        if (t % 2) a->m.ball.predictions[2] = a->m.ball.predictions[1];
+        memcpy(b, a, sizeof(cb::Match));
+        cb::ball_recalc(*a);
+        if (b->m.ball.validPredictions > 0 && b->m.ball.predictions[2] == b->m.ball.predictions[1]) (*shifted)++;
+        cb::ball_recalc_again(b->m.ball);
+        if (memcmp(&a->m.ball, &b->m.ball, sizeof(cb::Ball)) != 0) bad++;
+    }
+    free(a);
+    free(b);
+    return bad;
+}
+
 // The library's math functions on the host, for the per-function check against the reference's
 // restatements (tests/test_libm.py; numbering of libm_eval.cuh).
 extern "C" __attribute__((visibility("default"))) int hostsim_libm(int which, const double *x, const double *y,

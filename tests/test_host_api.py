@@ -682,3 +682,18 @@ def test_a_capped_loop_ends_the_step_with_the_undefined_path_error(host_library)
         assert batch.engine_state(1) != healthy  # the healthy environment stepped on
     finally:
         batch.close()
+
+
+def test_the_repeated_ball_prediction_shortcut_equals_a_second_prediction(host_library):
+    """ball_touch predicts the ball's flight twice on unchanged inputs; the build replaces the
+    second run by its exact outcome (touch.cuh: ball_recalc_again). On seeded balls on the ground,
+    in flight, at rest, against a post and in the goal's net, both give the same ball, byte for
+    byte: where the second run recomputes every entry, and where its cache shifts the list (half
+    the trials set up a ball that stays put between 10 and 20 ms)."""
+    import ctypes
+
+    lib = ctypes.CDLL(host_library)
+    shifted = ctypes.c_int()
+    bad = lib.hostsim_check_recalc_again(ctypes.c_uint(2024), 1000, ctypes.byref(shifted))
+    assert bad == 0
+    assert shifted.value >= 500
