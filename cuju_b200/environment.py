@@ -163,6 +163,7 @@ class BatchEnvironment:
             left = left if pair[0] is None else pair[0]
             right = right if pair[1] is None else pair[1]
             counts += [left, right]
+        self._requested = names
         self._paths = [p.encode() for p, _ in resolved]
         path_array = (ctypes.c_char_p * len(self._paths))(*self._paths)
         counts_array = (ctypes.c_int * len(counts))(*counts)
@@ -423,6 +424,35 @@ class BatchEnvironment:
         """The observation of every agent that the last reset or step wrote."""
         return self._outputs()[0]
 
+    def raw(self) -> dict[str, torch.Tensor]:
+        """GRF's raw observation of every agent from the last reset or step, one tensor per key
+        (python/cuju/_batch/environment.py:1268); views of the batch's buffer, which the next call
+        overwrites. Raises ConfigurationError unless the batch's representation is `raw`."""
+        if not self._raw:
+            raise ConfigurationError('expected a batch with the raw representation')
+        return self._raw_arrays('raw')
+
+    def final_raw(self) -> dict[str, torch.Tensor]:
+        """The raw observation of the step that ended each environment's last episode, as `raw`
+        returns it (python/cuju/_batch/environment.py:1278)."""
+        if not self._raw:
+            raise ConfigurationError('expected a batch with the raw representation')
+        return self._raw_arrays('final_raw')
+
+    @property
+    def scenario_name(self) -> str:
+        """The scenarios the batch was created with, by name without folders or suffixes, each
+        once, joined by ', ' (python/cuju/_batch/environment.py:710)."""
+        names = []
+        for asset in self._requested:
+            name = os.path.basename(os.fspath(asset))
+            for suffix in ('.cjb', '.py'):
+                if name.endswith(suffix):
+                    name = name[:-len(suffix)]
+            if name not in names:
+                names.append(name)
+        return ', '.join(names)
+
     def synchronize(self) -> None:
         with torch.cuda.device(self._torch_device):
             self._check(self._library.cuju_environment_synchronize(self._handle, self._stream()))
@@ -488,7 +518,10 @@ class BatchEnvironment:
         self._check(self._library.cuju_environment_episode(self._handle, index, values, None))
         return list(values)
 
+    @property
     def memory_bytes(self) -> int:
+        """The device bytes the batch holds, its tables included (a property, as
+        python/cuju/_batch/environment.py:885 has it)."""
         return int(self._library.cuju_environment_memory_bytes(self._handle))
 
     def close(self) -> None:

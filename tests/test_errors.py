@@ -48,3 +48,21 @@ def test_option_refusals_before_any_device():
 
     with pytest.raises(errors.MissingFileError):
         resolve_asset('no_such_scenario_l1_r0')
+
+
+def test_scenario_name_and_raw_accessors_without_a_device():
+    """The names a batch reports and the raw accessors' refusal, on a batch object built without
+    a device (only the attributes these read are set)."""
+    import pytest
+
+    from cuju_b200 import BatchEnvironment
+    from cuju_b200.errors import ConfigurationError
+
+    batch = BatchEnvironment.__new__(BatchEnvironment)
+    batch._requested = ['5_vs_5_l4_r0', '/some/dir/academy_attacker_vs_keeper_l0_r0.cjb', '5_vs_5_l4_r0']
+    batch._raw = False
+    assert batch.scenario_name == '5_vs_5_l4_r0, academy_attacker_vs_keeper_l0_r0'
+    with pytest.raises(ConfigurationError):
+        batch.raw()
+    with pytest.raises(ConfigurationError):
+        batch.final_raw()
